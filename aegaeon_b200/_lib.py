@@ -1,0 +1,178 @@
+"""ctypes binding of libkvx.so (the C ABI declared in include/kvx.h).
+
+The shared library is built in-tree (``aegaeon_b200/libkvx.so``, see
+``aegaeon_b200/build.py``).  There is no fallback: if it is missing, every
+entry point raises ``RuntimeError`` naming the build command.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libkvx.so")
+
+KVX_OK = 0
+KVX_ERR_INVALID_ARGUMENT = 1
+KVX_ERR_LENGTH_MISMATCH = 2
+KVX_ERR_GROUP = 3
+KVX_ERR_EXTENT = 4
+KVX_ERR_BLOCK_ID = 5
+KVX_ERR_HOST_MEMORY = 6
+KVX_ERR_CUDA = 7
+KVX_ERR_DEVICE_TIMEOUT = 8
+KVX_ERR_LAYOUT = 9
+KVX_ERR_NO_MEMORY = 10
+
+MODE_AUTO = 0
+MODE_SM = 1
+MODE_CE = 2
+MODE_SM_BULK = 3
+MODE_CE_EXTENT = 4
+MODE_NAMES = {
+    "auto": MODE_AUTO,
+    "sm": MODE_SM,
+    "ce": MODE_CE,
+    "sm_bulk": MODE_SM_BULK,
+    "ce_extent": MODE_CE_EXTENT,
+}
+
+_i64 = ctypes.c_int64
+_u64 = ctypes.c_uint64
+_int = ctypes.c_int
+_vp = ctypes.c_void_p
+_p_i64 = ctypes.POINTER(_i64)
+_p_u64 = ctypes.POINTER(_u64)
+
+# name -> (restype, argtypes); kept in the order of include/kvx.h.
+SIGNATURES = {
+    "kvx_status_string": (ctypes.c_char_p, [_int]),
+    "kvx_last_error": (ctypes.c_char_p, []),
+    "kvx_version": (_int, []),
+    "kvx_swap": (_int, [_p_i64, _p_i64, _i64, _int, _vp, _u64, _u64, _vp, _u64, _int, _vp]),
+    "kvx_layout_create": (
+        _int,
+        [_int, _i64, ctypes.POINTER(_vp), _p_u64, _p_u64, _p_u64, _p_u64, _i64, _p_i64,
+         _vp, _u64, _u64, _u64, ctypes.POINTER(_vp)],
+    ),
+    "kvx_layout_destroy": (_int, [_vp]),
+    "kvx_swap_blocks": (
+        _int,
+        [_vp, _i64, _p_i64, _p_i64, _p_i64, _p_i64, _p_i64, _int, _int, _vp, _p_u64, _p_u64],
+    ),
+    "kvx_migrate_blocks": (
+        _int,
+        [_vp, _vp, _i64, _p_i64, _p_i64, _p_i64, _p_i64, _p_i64, _int, _vp, _p_u64, _p_u64],
+    ),
+    "kvx_ipc_export": (_int, [_vp, ctypes.POINTER(ctypes.c_uint8), _p_u64]),
+    "kvx_ipc_import": (_int, [_int, ctypes.POINTER(ctypes.c_uint8), _u64, ctypes.POINTER(_vp)]),
+    "kvx_ipc_close": (_int, [_int, _vp]),
+    "kvx_upload_chunked": (_int, [_vp, _vp, _u64, _u64, _vp]),
+    "kvx_byte_extent": (_int, [_u64, _i64, _i64, _i64, _p_u64, _p_u64]),
+    "kvx_plan_swap_blocks": (
+        _int,
+        [_vp, _i64, _p_i64, _p_i64, _p_i64, _p_i64, _p_i64, _int, _p_u64, _p_u64, _p_u64, _p_i64],
+    ),
+    "kvx_plan_swap": (
+        _int,
+        [_p_i64, _p_i64, _i64, _int, _u64, _u64, _u64, _u64, _u64, _p_u64, _p_u64, _p_u64, _p_i64],
+    ),
+    "kvx_last_mode": (_int, []),
+    "kvx_device_status": (_int, [_int, _int, ctypes.POINTER(_int)]),
+    "kvx_configure": (_int, [_i64, _i64, _i64, _i64]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class KvxError(RuntimeError):
+    """A libkvx call failed with a CUDA or device-side error."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """Load libkvx.so once; raise if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            if not os.path.exists(LIB_PATH):
+                raise RuntimeError(
+                    f"{LIB_PATH} is missing; build it with "
+                    "`python -c 'import __graft_entry__ as g; g.build()'` "
+                    "or `python -m aegaeon_b200.build`"
+                )
+            handle = ctypes.CDLL(LIB_PATH)
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(handle, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = handle
+    return _lib
+
+
+def check(status: int) -> None:
+    """Map a kvx status to the exception type the reference raises."""
+    if status == KVX_OK:
+        return
+    msg = lib().kvx_last_error().decode(errors="replace") or lib().kvx_status_string(
+        status
+    ).decode()
+    if status in (KVX_ERR_LENGTH_MISMATCH, KVX_ERR_GROUP, KVX_ERR_EXTENT, KVX_ERR_LAYOUT):
+        raise ValueError(msg)
+    if status == KVX_ERR_BLOCK_ID:
+        raise IndexError(msg)
+    if status in (KVX_ERR_INVALID_ARGUMENT, KVX_ERR_HOST_MEMORY):
+        raise ValueError(msg)
+    raise KvxError(status, msg)
+
+
+def i64_array(values) -> ctypes.Array:
+    """Python ints (list/tuple/array/ndarray) -> contiguous int64 C array."""
+    try:
+        import numpy as np
+
+        if isinstance(values, np.ndarray):
+            a = np.ascontiguousarray(values, dtype=np.int64)
+            return (ctypes.c_int64 * a.size).from_buffer_copy(a)
+    except ImportError:  # pragma: no cover
+        pass
+    return (ctypes.c_int64 * len(values))(*values)
+
+
+def mode_of(mode) -> int:
+    if isinstance(mode, str):
+        try:
+            return MODE_NAMES[mode]
+        except KeyError:
+            raise ValueError(f"unknown transfer mode {mode!r}; one of {sorted(MODE_NAMES)}")
+    return int(mode)
+
+
+def last_mode_name() -> str:
+    m = lib().kvx_last_mode()
+    for k, v in MODE_NAMES.items():
+        if v == m:
+            return k
+    return str(m)
+
+
+def configure(sm_ctas_host: int = 0, sm_ctas_dev: int = 0, ce_min_run: int = 0,
+              staging_bytes: int = 0) -> None:
+    """Set the tuning knobs of the transfer-mode policy (0 keeps a value;
+    ce_min_run < 0 disables the copy-engine choice of the AUTO mode)."""
+    check(lib().kvx_configure(sm_ctas_host, sm_ctas_dev, ce_min_run, staging_bytes))
+
+
+def device_status(device: int, reset: bool = False) -> int:
+    """Device error word written by kernels whose bounded waits gave up."""
+    out = ctypes.c_int(0)
+    check(lib().kvx_device_status(device, 1 if reset else 0, ctypes.byref(out)))
+    return out.value

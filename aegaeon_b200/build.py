@@ -1,0 +1,64 @@
+"""Build libkvx.so in-tree for sm_100a with nvcc.
+
+``python -m aegaeon_b200.build`` (or ``__graft_entry__.build()``).  The
+library links the CUDA runtime statically so that it does not depend on which
+libcudart another extension in the process loaded first.
+"""
+
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+SOURCES = [
+    os.path.join(HERE, "csrc", "kvx_plan.cpp"),
+    os.path.join(HERE, "csrc", "kvx_runtime.cu"),
+]
+HEADERS = [
+    os.path.join(HERE, "csrc", "kvx_plan.h"),
+    os.path.join(HERE, "csrc", "kvx_kernels.cuh"),
+    os.path.join(ROOT, "include", "kvx.h"),
+]
+OUT = os.path.join(HERE, "libkvx.so")
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and os.path.exists(cand):
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def up_to_date() -> bool:
+    if not os.path.exists(OUT):
+        return False
+    t = os.path.getmtime(OUT)
+    return all(os.path.getmtime(p) <= t for p in SOURCES + HEADERS)
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and up_to_date():
+        return OUT
+    cmd = [
+        nvcc(), "-O3", "-std=c++17", *ARCH_FLAGS, "-lineinfo",
+        "-Xcompiler", "-fPIC,-Wall", "-shared", "-cudart", "static",
+        *SOURCES, "-o", OUT + ".tmp",
+    ]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stderr}\n{res.stdout}")
+    if verbose:
+        sys.stderr.write(res.stderr)
+    os.replace(OUT + ".tmp", OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

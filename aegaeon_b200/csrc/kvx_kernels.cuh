@@ -1,0 +1,251 @@
+// Copy kernels for KV-block movement on sm_100a.
+//
+// Both kernels walk a table of work items (kvx::Item: source, destination,
+// length, first tile).  The launch-wide tile sequence is split into one
+// contiguous span per CTA, so every CTA moves the same number of tiles and
+// streams through memory in order; a CTA finds its first item by binary search
+// and then advances item by item.
+//
+//  * kvx_copy_vec  : 16-byte vector loads and stores, eight in flight per
+//                    thread (32 KiB per 256-thread CTA).  Works on any memory
+//                    the SM can address: local HBM, device-mapped page-locked
+//                    host memory (PCIe) and IPC-mapped peer HBM (NVLink).
+//  * kvx_copy_bulk : local HBM only.  One elected thread runs a ring of TMA
+//                    bulk copies (cp.async.bulk global->shared completing on
+//                    an mbarrier, then shared->global in bulk groups).  Every
+//                    mbarrier wait is bounded by a %globaltimer deadline; on
+//                    expiry the kernel records KVX_ERR_DEVICE_TIMEOUT in the
+//                    device status word, drains its own bulk stores (also
+//                    bounded) and returns.  No multicast form is used.
+#pragma once
+
+#include <cstdint>
+
+#include "kvx_plan.h"
+
+namespace kvx {
+
+constexpr int kVecThreads = 256;
+constexpr int kVecUnroll = 8;  // 256 threads x 8 x 16 B = 32 KiB per pass
+
+enum SrcKind : int { kSrcDevice = 0, kSrcHost = 1 };
+
+__device__ __forceinline__ uint4 ld_dev16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ uint4 ld_host16(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cs.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void st16(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+// Largest i with items[i].tile_begin <= t (items sorted, items[0].tile_begin == 0).
+__device__ __forceinline__ uint32_t find_item(const Item* __restrict__ items,
+                                              uint32_t n_items, uint32_t t) {
+  uint32_t lo = 0, hi = n_items - 1;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi + 1) >> 1;
+    if (items[mid].tile_begin <= t)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ void cta_span(uint32_t n_tiles, uint32_t* t0,
+                                         uint32_t* t1) {
+  const uint32_t g = gridDim.x, b = blockIdx.x;
+  const uint32_t per = n_tiles / g, rem = n_tiles % g;
+  *t0 = b * per + min(b, rem);
+  *t1 = *t0 + per + (b < rem ? 1u : 0u);
+}
+
+template <int kSrc>
+__device__ __forceinline__ void cta_copy(const char* __restrict__ s,
+                                         char* __restrict__ d, uint32_t n) {
+  if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d) | n) &
+       15u) == 0) {
+    const uint32_t n16 = n >> 4;
+    const uint4* s16 = reinterpret_cast<const uint4*>(s);
+    uint4* d16 = reinterpret_cast<uint4*>(d);
+    for (uint32_t base = threadIdx.x; base < n16;
+         base += kVecThreads * kVecUnroll) {
+      uint4 r[kVecUnroll];
+#pragma unroll
+      for (int u = 0; u < kVecUnroll; ++u) {
+        const uint32_t k = base + u * kVecThreads;
+        if (k < n16) r[u] = kSrc == kSrcHost ? ld_host16(s16 + k) : ld_dev16(s16 + k);
+      }
+#pragma unroll
+      for (int u = 0; u < kVecUnroll; ++u) {
+        const uint32_t k = base + u * kVecThreads;
+        if (k < n16) st16(d16 + k, r[u]);
+      }
+    }
+  } else {
+    for (uint32_t k = threadIdx.x; k < n; k += kVecThreads) d[k] = s[k];
+  }
+}
+
+template <int kSrc>
+__global__ void __launch_bounds__(kVecThreads)
+    kvx_copy_vec(const Item* __restrict__ items, uint32_t n_items,
+                 uint32_t n_tiles, uint32_t tile_shift) {
+  uint32_t t0, t1;
+  cta_span(n_tiles, &t0, &t1);
+  if (t0 >= t1) return;
+  uint32_t i = find_item(items, n_items, t0);
+  for (uint32_t t = t0; t < t1; ++t) {
+    while (i + 1 < n_items && items[i + 1].tile_begin <= t) ++i;
+    const Item it = items[i];
+    const uint64_t off = uint64_t(t - it.tile_begin) << tile_shift;
+    const uint64_t left = uint64_t(it.len) - off;
+    const uint32_t n = uint32_t(min(left, uint64_t(1) << tile_shift));
+    cta_copy<kSrc>(reinterpret_cast<const char*>(it.src + off),
+                   reinterpret_cast<char*>(it.dst + off), n);
+  }
+}
+
+// ---- TMA bulk copy (local HBM only) ----------------------------------------
+
+constexpr int kBulkStages = 6;
+constexpr uint32_t kBulkChunk = 16384;  // one tile per stage
+constexpr uint32_t kBulkSmem = kBulkStages * kBulkChunk + kBulkStages * 8;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
+
+__device__ int g_kvx_device_status;
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait; false when the deadline passed.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  const uint64_t start = global_ns();
+  while (!mbar_try(bar, parity))
+    if (global_ns() - start > kWaitLimitNs) return false;
+  return true;
+}
+
+__device__ __forceinline__ void bulk_load(uint32_t smem, const void* src,
+                                          uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+      "r"(bytes)
+      : "memory");
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1], %2, [%3];" ::"r"(smem),
+      "l"(src), "r"(bytes), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_store(void* dst, uint32_t smem,
+                                           uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   dst),
+               "r"(smem), "r"(bytes)
+               : "memory");
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_read_le1() {
+  asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Requires every item 16-byte aligned in address and length (the host checks)
+// and tile size == kBulkChunk.
+__global__ void __launch_bounds__(32)
+    kvx_copy_bulk(const Item* __restrict__ items, uint32_t n_items,
+                  uint32_t n_tiles) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  if (threadIdx.x != 0) return;
+  uint32_t t0, t1;
+  cta_span(n_tiles, &t0, &t1);
+  if (t0 >= t1) return;
+  const uint32_t T = t1 - t0;
+  const uint32_t buf0 = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  const uint32_t bar0 = buf0 + kBulkStages * kBulkChunk;
+  for (int s = 0; s < kBulkStages; ++s)
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar0 + 8 * s)
+                 : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+
+  uint64_t st_dst[kBulkStages];
+  uint32_t st_len[kBulkStages];
+  uint32_t li = find_item(items, n_items, t0);  // load-side item cursor
+  uint32_t next_load = 0;                        // chunks issued so far
+  auto issue_load = [&]() {
+    const uint32_t k = next_load++;
+    const uint32_t t = t0 + k;
+    while (li + 1 < n_items && items[li + 1].tile_begin <= t) ++li;
+    const Item it = items[li];
+    const uint64_t off = uint64_t(t - it.tile_begin) * kBulkChunk;
+    const uint32_t n = uint32_t(min(uint64_t(it.len) - off, uint64_t(kBulkChunk)));
+    const int s = int(k % kBulkStages);
+    st_dst[s] = it.dst + off;
+    st_len[s] = n;
+    bulk_load(buf0 + s * kBulkChunk, reinterpret_cast<const void*>(it.src + off), n,
+              bar0 + 8 * s);
+  };
+
+  while (next_load < T && next_load < uint32_t(kBulkStages)) issue_load();
+  bool ok = true;
+  uint32_t k = 0;
+  for (; k < T; ++k) {
+    const int s = int(k % kBulkStages);
+    if (!mbar_wait(bar0 + 8 * s, (k / kBulkStages) & 1u)) {
+      ok = false;
+      break;
+    }
+    bulk_store(reinterpret_cast<void*>(st_dst[s]), buf0 + s * kBulkChunk, st_len[s]);
+    // Refill the stage of chunk k-1 once its store has read shared memory
+    // (every bulk group but the newest, store k, has finished reading).
+    if (k >= 1 && next_load < T) {
+      bulk_wait_read_le1();
+      issue_load();
+    }
+  }
+  bulk_wait_all();
+  if (!ok) {
+    atomicExch(&g_kvx_device_status, 8 /* KVX_ERR_DEVICE_TIMEOUT */);
+    // Let the loads still in flight into shared memory land, bounded.
+    for (uint32_t j = k; j < next_load; ++j)
+      if (!mbar_wait(bar0 + 8 * int(j % kBulkStages), (j / kBulkStages) & 1u)) break;
+  }
+}
+
+}  // namespace kvx

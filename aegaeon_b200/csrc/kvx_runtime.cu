@@ -1,0 +1,892 @@
+// C ABI of libkvx.so: per-device runtime state, transfer-mode selection and
+// the entry points declared in include/kvx.h.
+//
+// Execution model (all on the caller's stream, nothing synchronous unless a
+// library work area must be recycled):
+//   1. plan   : validate and turn the request into an ordered copy list
+//               (kvx_plan.cpp), split into conflict-free waves, coalesce;
+//   2. upload : write the kernel item table into a page-locked descriptor ring
+//               and queue one host->device copy of it;
+//   3. launch : one copy kernel per wave (SM mode), or per staging chunk a
+//               gather/scatter kernel plus copy-engine copies (CE mode);
+//   4. fence  : record a pooled event on the stream that frees the ring
+//               region (and the staging area) for reuse.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <deque>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/kvx.h"
+#include "kvx_kernels.cuh"
+#include "kvx_plan.h"
+
+namespace kvx {
+namespace {
+
+thread_local std::string t_last_error;
+thread_local int t_last_mode = 0;
+
+int set_error(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+int cuda_error(cudaError_t e, const char* what) {
+  std::string m = std::string(what) + ": " + cudaGetErrorName(e) + " (" +
+                  cudaGetErrorString(e) + ")";
+  return set_error(KVX_ERR_CUDA, m);
+}
+
+#define KVX_CUDA(call)                                  \
+  do {                                                  \
+    cudaError_t e_ = (call);                            \
+    if (e_ != cudaSuccess) return cuda_error(e_, #call); \
+  } while (0)
+
+int from_plan(const Error& e) {
+  if (e.ok()) return KVX_OK;
+  return set_error(e.code, e.msg);
+}
+
+// ---- tunables ----------------------------------------------------------------
+struct Tunables {
+  int64_t sm_ctas_host = 0;    // 0: number of SMs
+  int64_t sm_ctas_dev = 0;     // 0: 8 x number of SMs
+  int64_t ce_min_run = 8ll << 20;
+  int64_t staging_bytes = 256ll << 20;
+};
+std::mutex g_tun_mu;
+Tunables g_tun;
+
+int64_t env_i64(const char* name, int64_t dflt) {
+  const char* v = std::getenv(name);
+  if (!v || !*v) return dflt;
+  return std::strtoll(v, nullptr, 0);
+}
+
+Tunables tunables() {
+  static std::once_flag once;
+  std::call_once(once, [] {
+    std::lock_guard<std::mutex> g(g_tun_mu);
+    g_tun.sm_ctas_host = env_i64("KVX_SM_CTAS_HOST", g_tun.sm_ctas_host);
+    g_tun.sm_ctas_dev = env_i64("KVX_SM_CTAS_DEV", g_tun.sm_ctas_dev);
+    g_tun.ce_min_run = env_i64("KVX_CE_MIN_RUN", g_tun.ce_min_run);
+    g_tun.staging_bytes = env_i64("KVX_STAGING_BYTES", g_tun.staging_bytes);
+  });
+  std::lock_guard<std::mutex> g(g_tun_mu);
+  return g_tun;
+}
+
+// ---- per-device state ---------------------------------------------------------
+struct Region {
+  cudaEvent_t ev;
+  size_t begin, end;
+};
+
+struct Staging {
+  char* dev = nullptr;
+  size_t cap = 0;
+  cudaEvent_t last = nullptr;  // recorded after the latest use
+  bool used = false;
+};
+
+struct DeviceState {
+  int device = 0;
+  int sms = 148;
+  std::mutex mu;
+  // Descriptor ring: page-locked host + device copies of item tables.
+  char* ring_host = nullptr;
+  char* ring_dev = nullptr;
+  size_t ring_cap = 0;
+  size_t ring_head = 0;
+  std::deque<Region> inflight;
+  std::vector<cudaEvent_t> pool;
+  Staging staging[2];  // [0] device->host, [1] host->device
+  bool bulk_ready = false;
+};
+
+std::mutex g_dev_mu;
+DeviceState* g_devs[64] = {};
+
+class DeviceGuard {
+ public:
+  explicit DeviceGuard(int dev) {
+    if (cudaGetDevice(&prev_) != cudaSuccess) prev_ = -1;
+    if (prev_ != dev) {
+      ok_ = cudaSetDevice(dev) == cudaSuccess;
+      switched_ = true;
+    }
+  }
+  ~DeviceGuard() {
+    if (switched_ && prev_ >= 0) cudaSetDevice(prev_);
+  }
+  bool ok() const { return ok_; }
+
+ private:
+  int prev_ = -1;
+  bool switched_ = false;
+  bool ok_ = true;
+};
+
+int get_state(int device, DeviceState** out) {
+  if (device < 0 || device >= 64)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "device index out of range");
+  std::lock_guard<std::mutex> g(g_dev_mu);
+  if (!g_devs[device]) {
+    int sms = 0;
+    cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    if (e != cudaSuccess) return cuda_error(e, "cudaDeviceGetAttribute");
+    auto* st = new DeviceState();
+    st->device = device;
+    st->sms = sms;
+    g_devs[device] = st;
+  }
+  *out = g_devs[device];
+  return KVX_OK;
+}
+
+int take_event(DeviceState* st, cudaEvent_t* ev) {
+  if (!st->pool.empty()) {
+    *ev = st->pool.back();
+    st->pool.pop_back();
+    return KVX_OK;
+  }
+  KVX_CUDA(cudaEventCreateWithFlags(ev, cudaEventDisableTiming));
+  return KVX_OK;
+}
+
+int retire_front(DeviceState* st, bool block) {
+  Region r = st->inflight.front();
+  if (block) {
+    KVX_CUDA(cudaEventSynchronize(r.ev));
+  } else {
+    cudaError_t q = cudaEventQuery(r.ev);
+    if (q == cudaErrorNotReady) return 1;
+    if (q != cudaSuccess) return cuda_error(q, "cudaEventQuery");
+  }
+  st->inflight.pop_front();
+  st->pool.push_back(r.ev);
+  return KVX_OK;
+}
+
+// Reserve `bytes` of the descriptor ring; returns the offset.
+int ring_acquire(DeviceState* st, size_t bytes, size_t* off) {
+  bytes = (bytes + 255) & ~size_t(255);
+  if (bytes > st->ring_cap) {
+    while (!st->inflight.empty()) {
+      int rc = retire_front(st, true);
+      if (rc) return rc;
+    }
+    if (st->ring_host) cudaFreeHost(st->ring_host);
+    if (st->ring_dev) cudaFree(st->ring_dev);
+    st->ring_host = st->ring_dev = nullptr;
+    size_t cap = std::max<size_t>(bytes * 2, size_t(8) << 20);
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&st->ring_host), cap,
+                                  cudaHostAllocDefault);
+    if (e != cudaSuccess) return cuda_error(e, "cudaHostAlloc(descriptor ring)");
+    e = cudaMalloc(reinterpret_cast<void**>(&st->ring_dev), cap);
+    if (e != cudaSuccess) {
+      cudaFreeHost(st->ring_host);
+      st->ring_host = nullptr;
+      return cuda_error(e, "cudaMalloc(descriptor ring)");
+    }
+    st->ring_cap = cap;
+    st->ring_head = 0;
+  }
+  while (!st->inflight.empty()) {  // reclaim finished regions, non-blocking
+    int rc = retire_front(st, false);
+    if (rc == 1) break;
+    if (rc) return rc;
+  }
+  size_t start = st->ring_head;
+  if (start + bytes > st->ring_cap) start = 0;
+  for (;;) {
+    bool clash = false;
+    for (const Region& r : st->inflight)
+      if (r.begin < start + bytes && start < r.end) {
+        clash = true;
+        break;
+      }
+    if (!clash) break;
+    int rc = retire_front(st, true);
+    if (rc) return rc;
+  }
+  st->ring_head = start + bytes;
+  *off = start;
+  return KVX_OK;
+}
+
+int ring_release_on(DeviceState* st, size_t off, size_t bytes, cudaStream_t s) {
+  cudaEvent_t ev;
+  int rc = take_event(st, &ev);
+  if (rc) return rc;
+  KVX_CUDA(cudaEventRecord(ev, s));
+  st->inflight.push_back(Region{ev, off, off + ((bytes + 255) & ~size_t(255))});
+  return KVX_OK;
+}
+
+int staging_get(DeviceState* st, int idx, size_t want, cudaStream_t s,
+                Staging** out) {
+  Staging& sg = st->staging[idx];
+  if (!sg.dev || sg.cap < want) {
+    if (sg.dev) {
+      if (sg.used) KVX_CUDA(cudaEventSynchronize(sg.last));
+      cudaFree(sg.dev);
+      sg.dev = nullptr;
+    }
+    cudaError_t e = cudaMalloc(reinterpret_cast<void**>(&sg.dev), want);
+    if (e != cudaSuccess) return cuda_error(e, "cudaMalloc(staging)");
+    sg.cap = want;
+    sg.used = false;
+    if (!sg.last) KVX_CUDA(cudaEventCreateWithFlags(&sg.last, cudaEventDisableTiming));
+  }
+  if (sg.used) KVX_CUDA(cudaStreamWaitEvent(s, sg.last, 0));
+  *out = &sg;
+  return KVX_OK;
+}
+
+// ---- kernel launch ---------------------------------------------------------
+enum class Path { kHostSrc, kHostDst, kDevice, kPeer };
+
+int ctas_for(const DeviceState* st, Path p, const Tunables& tn) {
+  if (p == Path::kHostSrc || p == Path::kHostDst)
+    return int(tn.sm_ctas_host > 0 ? tn.sm_ctas_host : st->sms);
+  return int(tn.sm_ctas_dev > 0 ? tn.sm_ctas_dev : 8 * st->sms);
+}
+
+bool all_aligned16(const std::vector<Copy>& v) {
+  for (const Copy& c : v)
+    if ((c.src | c.dst | c.len) & 15) return false;
+  return true;
+}
+
+// Item table of several launches, uploaded once.
+struct Launch {
+  size_t item_off;   // index into the combined item vector
+  uint32_t n_items;
+  uint32_t n_tiles;
+  bool bulk;
+  Path path;
+};
+
+int upload_items(DeviceState* st, const std::vector<Item>& items,
+                 cudaStream_t s, size_t* ring_off) {
+  const size_t bytes = items.size() * sizeof(Item);
+  int rc = ring_acquire(st, bytes ? bytes : 256, ring_off);
+  if (rc) return rc;
+  if (bytes) {
+    std::memcpy(st->ring_host + *ring_off, items.data(), bytes);
+    KVX_CUDA(cudaMemcpyAsync(st->ring_dev + *ring_off, st->ring_host + *ring_off,
+                             bytes, cudaMemcpyHostToDevice, s));
+  }
+  return KVX_OK;
+}
+
+int ensure_bulk(DeviceState* st) {
+  if (st->bulk_ready) return KVX_OK;
+  KVX_CUDA(cudaFuncSetAttribute(kvx_copy_bulk,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(kBulkSmem)));
+  st->bulk_ready = true;
+  return KVX_OK;
+}
+
+int launch_one(DeviceState* st, const Item* dev_items, const Launch& l,
+               cudaStream_t s, const Tunables& tn) {
+  if (l.n_tiles == 0) return KVX_OK;
+  if (l.bulk) {
+    int rc = ensure_bulk(st);
+    if (rc) return rc;
+    // Two 96 KiB CTAs fit on an SM.
+    const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(2 * st->sms));
+    kvx_copy_bulk<<<grid, 32, kBulkSmem, s>>>(dev_items, l.n_items, l.n_tiles);
+  } else {
+    const uint32_t grid =
+        std::min<uint32_t>(l.n_tiles, uint32_t(ctas_for(st, l.path, tn)));
+    if (l.path == Path::kHostSrc)
+      kvx_copy_vec<kSrcHost><<<grid, kVecThreads, 0, s>>>(dev_items, l.n_items,
+                                                          l.n_tiles, 15);
+    else
+      kvx_copy_vec<kSrcDevice><<<grid, kVecThreads, 0, s>>>(dev_items, l.n_items,
+                                                            l.n_tiles, 15);
+  }
+  KVX_CUDA(cudaGetLastError());
+  return KVX_OK;
+}
+
+constexpr uint32_t kVecTile = 1u << 15;  // 32 KiB
+
+// Run waves of device-visible copies through the SM kernels (one launch per
+// wave, one descriptor upload for all of them).
+int run_sm(DeviceState* st, const std::vector<Copy>& copies,
+           const std::vector<size_t>& waves, Path path, bool allow_bulk,
+           cudaStream_t s, const Tunables& tn) {
+  std::vector<Item> all;
+  std::vector<Launch> launches;
+  std::vector<Item> tmp;
+  size_t begin = 0;
+  for (size_t end : waves) {
+    std::vector<Copy> w(copies.begin() + begin, copies.begin() + end);
+    begin = end;
+    coalesce(&w);
+    const bool bulk = allow_bulk && path == Path::kDevice && all_aligned16(w);
+    const uint64_t tiles = build_items(w, bulk ? kBulkChunk : kVecTile, &tmp);
+    if (tiles > 0xffffffffull)
+      return set_error(KVX_ERR_INVALID_ARGUMENT, "request too large for one launch");
+    launches.push_back(Launch{all.size(), uint32_t(tmp.size()), uint32_t(tiles), bulk, path});
+    all.insert(all.end(), tmp.begin(), tmp.end());
+  }
+  size_t off = 0;
+  int rc = upload_items(st, all, s, &off);
+  if (rc) return rc;
+  const Item* base = reinterpret_cast<const Item*>(st->ring_dev + off);
+  for (const Launch& l : launches) {
+    rc = launch_one(st, base + l.item_off, l, s, tn);
+    if (rc) return rc;
+  }
+  return ring_release_on(st, off, all.size() * sizeof(Item), s);
+}
+
+// Copy-engine path through a staging area.  `copies` use the caller's host
+// addresses; host_is_src selects the direction.
+int run_ce_staged(DeviceState* st, const std::vector<Copy>& copies,
+                  const std::vector<size_t>& waves, bool host_is_src,
+                  bool allow_bulk, cudaStream_t s, const Tunables& tn) {
+  const size_t cap = size_t(std::max<int64_t>(tn.staging_bytes, 1 << 20)) & ~size_t(4095);
+  uint64_t total = 0;
+  for (const Copy& c : copies) total += c.len;
+  if (total == 0) return KVX_OK;
+  Staging* sg = nullptr;
+  int rc = staging_get(st, host_is_src ? 1 : 0, cap, s, &sg);
+  if (rc) return rc;
+  const uint64_t sbase = reinterpret_cast<uint64_t>(sg->dev);
+  // Build every chunk's item table first (one upload).
+  std::vector<std::vector<StagedChunk>> plans;
+  std::vector<Item> all, tmp;
+  std::vector<Launch> launches;
+  size_t begin = 0;
+  for (size_t end : waves) {
+    std::vector<Copy> w(copies.begin() + begin, copies.begin() + end);
+    begin = end;
+    std::vector<StagedChunk> chunks;
+    plan_staged(w, host_is_src, sg->cap, &chunks);
+    for (StagedChunk& ch : chunks) {
+      for (Copy& m : ch.device_moves) (host_is_src ? m.src : m.dst) += sbase;
+      const bool bulk = allow_bulk && all_aligned16(ch.device_moves);
+      const uint64_t tiles = build_items(ch.device_moves, bulk ? kBulkChunk : kVecTile, &tmp);
+      launches.push_back(Launch{all.size(), uint32_t(tmp.size()), uint32_t(tiles), bulk,
+                                Path::kDevice});
+      all.insert(all.end(), tmp.begin(), tmp.end());
+    }
+    plans.push_back(std::move(chunks));
+  }
+  size_t off = 0;
+  rc = upload_items(st, all, s, &off);
+  if (rc) return rc;
+  const Item* base = reinterpret_cast<const Item*>(st->ring_dev + off);
+  size_t li = 0;
+  for (const auto& chunks : plans) {
+    for (const StagedChunk& ch : chunks) {
+      const Launch& l = launches[li++];
+      if (host_is_src) {
+        for (const Copy& r : ch.host_runs)
+          KVX_CUDA(cudaMemcpyAsync(sg->dev + r.dst, reinterpret_cast<const void*>(r.src),
+                                   r.len, cudaMemcpyHostToDevice, s));
+        rc = launch_one(st, base + l.item_off, l, s, tn);
+        if (rc) return rc;
+      } else {
+        rc = launch_one(st, base + l.item_off, l, s, tn);
+        if (rc) return rc;
+        for (const Copy& r : ch.host_runs)
+          KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.dst), sg->dev + r.src,
+                                   r.len, cudaMemcpyDeviceToHost, s));
+      }
+    }
+  }
+  KVX_CUDA(cudaEventRecord(sg->last, s));
+  sg->used = true;
+  return ring_release_on(st, off, all.size() * sizeof(Item), s);
+}
+
+// One copy-engine copy per coalesced extent (no staging, no kernel).
+int run_ce_extent(const std::vector<Copy>& copies, const std::vector<size_t>& waves,
+                  cudaStream_t s) {
+  size_t begin = 0;
+  for (size_t end : waves) {
+    std::vector<Copy> w(copies.begin() + begin, copies.begin() + end);
+    begin = end;
+    coalesce(&w);
+    for (const Copy& c : w)
+      KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(c.dst),
+                               reinterpret_cast<const void*>(c.src), c.len,
+                               cudaMemcpyDefault, s));
+  }
+  return KVX_OK;
+}
+
+// Host memory facts for the SM path.
+struct HostInfo {
+  bool mapped = false;     // device can address it
+  uint64_t dev_base = 0;   // device-visible address of `ptr`
+};
+
+HostInfo host_info(const void* ptr, int device) {
+  HostInfo h;
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return h;
+  }
+  if (a.type == cudaMemoryTypeHost && a.devicePointer) {
+    h.mapped = true;
+    h.dev_base = reinterpret_cast<uint64_t>(a.devicePointer);
+  } else if (a.type == cudaMemoryTypeManaged) {
+    h.mapped = true;
+    h.dev_base = reinterpret_cast<uint64_t>(ptr);
+  }
+  (void)device;
+  return h;
+}
+
+int check_device_memory(const void* ptr, int device, const char* what) {
+  cudaPointerAttributes a;
+  cudaError_t e = cudaPointerGetAttributes(&a, ptr);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(KVX_ERR_INVALID_ARGUMENT, std::string(what) + " is not CUDA memory");
+  }
+  if (a.type != cudaMemoryTypeDevice && a.type != cudaMemoryTypeManaged)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, std::string(what) + " is not device memory");
+  if (a.type == cudaMemoryTypeDevice && a.device != device)
+    return set_error(KVX_ERR_INVALID_ARGUMENT,
+                     std::string(what) + " lives on device " + std::to_string(a.device) +
+                         ", not on the current device " + std::to_string(device));
+  return KVX_OK;
+}
+
+// Execute host<->device copies (caller host addresses) in the chosen mode.
+int execute_host_copies(DeviceState* st, std::vector<Copy>& copies, bool is_swap_in,
+                        const HostInfo& hi, uint64_t host_caller_base, int mode,
+                        cudaStream_t s) {
+  const Tunables tn = tunables();
+  if (copies.empty()) {
+    t_last_mode = mode == KVX_MODE_AUTO ? KVX_MODE_SM : mode;
+    return KVX_OK;
+  }
+  if (mode == KVX_MODE_AUTO) {
+    if (!hi.mapped) {
+      mode = KVX_MODE_CE;
+    } else {
+      const uint64_t run = mean_host_run(copies, is_swap_in);
+      mode = (tn.ce_min_run > 0 && run >= uint64_t(tn.ce_min_run)) ? KVX_MODE_CE : KVX_MODE_SM;
+    }
+  }
+  if (mode == KVX_MODE_SM_BULK) mode = KVX_MODE_SM;  // bulk is device-only
+  const std::vector<size_t> waves = split_waves(copies);
+  int rc;
+  if (mode == KVX_MODE_SM) {
+    if (!hi.mapped)
+      return set_error(KVX_ERR_HOST_MEMORY,
+                       "host buffer is not page-locked/device-mapped; the SM mode "
+                       "needs cudaHostAlloc or cudaHostRegister memory");
+    const uint64_t delta = hi.dev_base - host_caller_base;  // modular
+    for (Copy& c : copies) (is_swap_in ? c.src : c.dst) += delta;
+    rc = run_sm(st, copies, waves, is_swap_in ? Path::kHostSrc : Path::kHostDst, false, s, tn);
+  } else if (mode == KVX_MODE_CE) {
+    rc = run_ce_staged(st, copies, waves, is_swap_in, true, s, tn);
+  } else if (mode == KVX_MODE_CE_EXTENT) {
+    rc = run_ce_extent(copies, waves, s);
+  } else {
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "unknown transfer mode " + std::to_string(mode));
+  }
+  if (rc == KVX_OK) t_last_mode = mode;
+  return rc;
+}
+
+}  // namespace
+}  // namespace kvx
+
+struct kvx_layout {
+  kvx::Layout L;
+  kvx::HostInfo host;
+};
+
+using namespace kvx;
+
+extern "C" {
+
+const char* kvx_status_string(int status) {
+  switch (status) {
+    case KVX_OK: return "ok";
+    case KVX_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case KVX_ERR_LENGTH_MISMATCH: return "metadata length mismatch";
+    case KVX_ERR_GROUP: return "invalid cache-group id";
+    case KVX_ERR_EXTENT: return "invalid kernel-block extent";
+    case KVX_ERR_BLOCK_ID: return "block id out of range";
+    case KVX_ERR_HOST_MEMORY: return "host memory not usable";
+    case KVX_ERR_CUDA: return "CUDA error";
+    case KVX_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case KVX_ERR_LAYOUT: return "layouts differ";
+    case KVX_ERR_NO_MEMORY: return "out of memory";
+    default: return "unknown status";
+  }
+}
+
+const char* kvx_last_error(void) { return t_last_error.c_str(); }
+int kvx_version(void) { return 10000; }
+int kvx_last_mode(void) { return t_last_mode; }
+
+int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev, int64_t ce_min_run,
+                  int64_t staging_bytes) {
+  tunables();
+  std::lock_guard<std::mutex> g(g_tun_mu);
+  if (sm_ctas_host > 0) g_tun.sm_ctas_host = sm_ctas_host;
+  if (sm_ctas_dev > 0) g_tun.sm_ctas_dev = sm_ctas_dev;
+  if (ce_min_run != 0) g_tun.ce_min_run = ce_min_run < 0 ? 0 : ce_min_run;
+  if (staging_bytes > 0) g_tun.staging_bytes = staging_bytes;
+  return KVX_OK;
+}
+
+int kvx_byte_extent(uint64_t page_bytes, int64_t kernel_blocks_per_page,
+                    int64_t first_kernel_block, int64_t num_kernel_blocks,
+                    uint64_t* byte_offset_out, uint64_t* byte_length_out) {
+  t_last_error.clear();
+  if (!byte_offset_out || !byte_length_out)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "null output pointer");
+  return from_plan(byte_extent(page_bytes, kernel_blocks_per_page, first_kernel_block,
+                               num_kernel_blocks, byte_offset_out, byte_length_out));
+}
+
+int kvx_plan_swap(const int64_t* source_block_ids, const int64_t* target_block_ids,
+                  int64_t num_ids, int is_swap_in, uint64_t kv_cache,
+                  uint64_t kv_cache_bytes, uint64_t block_bytes, uint64_t kv_swap,
+                  uint64_t kv_swap_bytes, uint64_t* src_addrs, uint64_t* dst_addrs,
+                  uint64_t* lengths, int64_t* num_copies_inout) {
+  t_last_error.clear();
+  if (!num_copies_inout) return set_error(KVX_ERR_INVALID_ARGUMENT, "null count");
+  std::vector<Copy> copies;
+  int rc = from_plan(plan_swap(source_block_ids, target_block_ids, num_ids, is_swap_in != 0,
+                               kv_cache, kv_cache_bytes, block_bytes, kv_swap,
+                               kv_swap_bytes, &copies));
+  if (rc) return rc;
+  const int64_t cap = *num_copies_inout;
+  *num_copies_inout = int64_t(copies.size());
+  if (cap < int64_t(copies.size()) || !src_addrs || !dst_addrs || !lengths) return KVX_OK;
+  for (size_t i = 0; i < copies.size(); ++i) {
+    src_addrs[i] = copies[i].src;
+    dst_addrs[i] = copies[i].dst;
+    lengths[i] = copies[i].len;
+  }
+  return KVX_OK;
+}
+
+int kvx_swap(const int64_t* source_block_ids, const int64_t* target_block_ids,
+             int64_t num_ids, int is_swap_in, void* kv_cache, uint64_t kv_cache_bytes,
+             uint64_t block_bytes, void* kv_swap, uint64_t kv_swap_bytes, int mode,
+             void* stream) {
+  t_last_error.clear();
+  std::vector<Copy> copies;
+  int rc = from_plan(plan_swap(source_block_ids, target_block_ids, num_ids, is_swap_in != 0,
+                               reinterpret_cast<uint64_t>(kv_cache), kv_cache_bytes,
+                               block_bytes, reinterpret_cast<uint64_t>(kv_swap),
+                               kv_swap_bytes, &copies));
+  if (rc) return rc;
+  if (copies.empty()) {
+    t_last_mode = mode == KVX_MODE_AUTO ? KVX_MODE_SM : mode;
+    return KVX_OK;
+  }
+  int device = 0;
+  KVX_CUDA(cudaGetDevice(&device));
+  rc = check_device_memory(kv_cache, device, "kv_cache");
+  if (rc) return rc;
+  DeviceState* st = nullptr;
+  rc = get_state(device, &st);
+  if (rc) return rc;
+  const HostInfo hi = host_info(kv_swap, device);
+  std::lock_guard<std::mutex> g(st->mu);
+  return execute_host_copies(st, copies, is_swap_in != 0, hi,
+                             reinterpret_cast<uint64_t>(kv_swap), mode,
+                             reinterpret_cast<cudaStream_t>(stream));
+}
+
+int kvx_layout_create(int device, int64_t num_segments, void* const* segment_pages,
+                      const uint64_t* segment_page_bytes, const uint64_t* segment_num_blocks,
+                      const uint64_t* segment_cpu_offsets,
+                      const uint64_t* segment_owner_masks, int64_t num_groups,
+                      const int64_t* group_blocks_per_kv_block, void* host_pool,
+                      uint64_t host_pool_bytes, uint64_t host_row_bytes,
+                      uint64_t host_row_offset, kvx_layout** layout_out) {
+  t_last_error.clear();
+  if (!layout_out) return set_error(KVX_ERR_INVALID_ARGUMENT, "null layout_out");
+  *layout_out = nullptr;
+  if (num_segments < 0 || num_groups < 0)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "negative table size");
+  if (num_segments > 0 && (!segment_pages || !segment_page_bytes || !segment_num_blocks ||
+                           !segment_cpu_offsets || !segment_owner_masks))
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "null segment table");
+  if (num_groups > 0 && !group_blocks_per_kv_block)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "null group table");
+  auto lay = std::make_unique<kvx_layout>();
+  Layout& L = lay->L;
+  L.device = device;
+  for (int64_t s = 0; s < num_segments; ++s) {
+    L.seg_pages.push_back(reinterpret_cast<uint64_t>(segment_pages[s]));
+    L.seg_page_bytes.push_back(segment_page_bytes[s]);
+    L.seg_num_blocks.push_back(segment_num_blocks[s]);
+    L.seg_cpu_offset.push_back(segment_cpu_offsets[s]);
+    L.seg_owner_mask.push_back(segment_owner_masks[s]);
+  }
+  L.group_ratio.assign(group_blocks_per_kv_block, group_blocks_per_kv_block + num_groups);
+  L.host_pool = reinterpret_cast<uint64_t>(host_pool);
+  L.host_pool_bytes = host_pool ? host_pool_bytes : 0;
+  L.host_row_bytes = host_pool ? host_row_bytes : 0;
+  L.host_row_offset = host_pool ? host_row_offset : 0;
+  L.host_num_rows = (host_pool && host_row_bytes) ? host_pool_bytes / host_row_bytes : 0;
+  int rc = from_plan(validate_layout(L));
+  if (rc) return rc;
+  if (host_pool) {
+    // Best effort: a CPU-only process (no driver) still gets a layout usable
+    // for planning; the copy entry points re-check the mapping.
+    lay->host = host_info(host_pool, device);
+    L.host_pool_dev = lay->host.mapped ? lay->host.dev_base : 0;
+  }
+  *layout_out = lay.release();
+  return KVX_OK;
+}
+
+int kvx_layout_destroy(kvx_layout* layout) {
+  delete layout;
+  return KVX_OK;
+}
+
+int kvx_plan_swap_blocks(const kvx_layout* layout, int64_t num_entries,
+                         const int64_t* source_block_ids, const int64_t* target_block_ids,
+                         const int64_t* group_ids, const int64_t* first_kernel_blocks,
+                         const int64_t* valid_kernel_blocks, int is_swap_in,
+                         uint64_t* src_addrs, uint64_t* dst_addrs, uint64_t* lengths,
+                         int64_t* num_copies_inout) {
+  t_last_error.clear();
+  if (!layout || !num_copies_inout)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "null layout or count");
+  Entries e{num_entries, source_block_ids, target_block_ids, group_ids,
+            first_kernel_blocks, valid_kernel_blocks};
+  std::vector<Copy> copies;
+  int rc = from_plan(plan_swap_blocks(layout->L, e, is_swap_in != 0, layout->L.host_pool,
+                                      &copies, nullptr));
+  if (rc) return rc;
+  const int64_t cap = *num_copies_inout;
+  *num_copies_inout = int64_t(copies.size());
+  if (cap < int64_t(copies.size()) || !src_addrs || !dst_addrs || !lengths) return KVX_OK;
+  for (size_t i = 0; i < copies.size(); ++i) {
+    src_addrs[i] = copies[i].src;
+    dst_addrs[i] = copies[i].dst;
+    lengths[i] = copies[i].len;
+  }
+  return KVX_OK;
+}
+
+int kvx_swap_blocks(kvx_layout* layout, int64_t num_entries,
+                    const int64_t* source_block_ids, const int64_t* target_block_ids,
+                    const int64_t* group_ids, const int64_t* first_kernel_blocks,
+                    const int64_t* valid_kernel_blocks, int is_swap_in, int mode,
+                    void* stream, uint64_t* copied_bytes, uint64_t* copy_extents) {
+  t_last_error.clear();
+  if (!layout) return set_error(KVX_ERR_INVALID_ARGUMENT, "null layout");
+  Entries e{num_entries, source_block_ids, target_block_ids, group_ids,
+            first_kernel_blocks, valid_kernel_blocks};
+  std::vector<Copy> copies;
+  uint64_t copied = 0;
+  int rc = from_plan(plan_swap_blocks(layout->L, e, is_swap_in != 0, layout->L.host_pool,
+                                      &copies, &copied));
+  if (rc) return rc;
+  if (copied_bytes) *copied_bytes = copied;
+  if (copy_extents) *copy_extents = copies.size();
+  if (copies.empty()) {
+    t_last_mode = mode == KVX_MODE_AUTO ? KVX_MODE_SM : mode;
+    return KVX_OK;
+  }
+  DeviceGuard dg(layout->L.device);
+  if (!dg.ok()) return set_error(KVX_ERR_CUDA, "cannot select the layout's device");
+  DeviceState* st = nullptr;
+  rc = get_state(layout->L.device, &st);
+  if (rc) return rc;
+  if (!layout->host.mapped) {  // re-query: the pool may have been registered since
+    layout->host = host_info(reinterpret_cast<void*>(layout->L.host_pool), layout->L.device);
+    layout->L.host_pool_dev = layout->host.mapped ? layout->host.dev_base : 0;
+  }
+  std::lock_guard<std::mutex> g(st->mu);
+  return execute_host_copies(st, copies, is_swap_in != 0, layout->host, layout->L.host_pool,
+                             mode, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int kvx_migrate_blocks(kvx_layout* source, kvx_layout* target, int64_t num_entries,
+                       const int64_t* source_block_ids, const int64_t* target_block_ids,
+                       const int64_t* group_ids, const int64_t* first_kernel_blocks,
+                       const int64_t* valid_kernel_blocks, int mode, void* stream,
+                       uint64_t* copied_bytes, uint64_t* copy_extents) {
+  t_last_error.clear();
+  if (!source || !target) return set_error(KVX_ERR_INVALID_ARGUMENT, "null layout");
+  Entries e{num_entries, source_block_ids, target_block_ids, group_ids,
+            first_kernel_blocks, valid_kernel_blocks};
+  std::vector<Copy> copies;
+  uint64_t copied = 0;
+  int rc = from_plan(plan_migrate(source->L, target->L, e, &copies, &copied));
+  if (rc) return rc;
+  if (copied_bytes) *copied_bytes = copied;
+  if (copy_extents) *copy_extents = copies.size();
+  if (copies.empty()) {
+    t_last_mode = mode == KVX_MODE_AUTO ? KVX_MODE_SM : mode;
+    return KVX_OK;
+  }
+  int device = 0;
+  KVX_CUDA(cudaGetDevice(&device));
+  DeviceState* st = nullptr;
+  rc = get_state(device, &st);
+  if (rc) return rc;
+  // Local when every page table base of both layouts is memory of this GPU;
+  // otherwise some side is a peer mapping and only the vector kernel is used.
+  bool local = true;
+  for (const kvx_layout* lay : {source, target})
+    for (uint64_t p : lay->L.seg_pages) {
+      cudaPointerAttributes a;
+      if (cudaPointerGetAttributes(&a, reinterpret_cast<void*>(p)) != cudaSuccess) {
+        cudaGetLastError();
+        return set_error(KVX_ERR_INVALID_ARGUMENT, "segment pages are not CUDA memory");
+      }
+      if (a.type != cudaMemoryTypeDevice)
+        return set_error(KVX_ERR_INVALID_ARGUMENT, "segment pages are not device memory");
+      if (a.device != device) local = false;
+    }
+  const Tunables tn = tunables();
+  std::lock_guard<std::mutex> g(st->mu);
+  const std::vector<size_t> waves = split_waves(copies);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (mode == KVX_MODE_AUTO) mode = KVX_MODE_SM;
+  if (mode == KVX_MODE_CE || mode == KVX_MODE_CE_EXTENT) {
+    rc = run_ce_extent(copies, waves, s);
+    mode = KVX_MODE_CE_EXTENT;
+  } else if (mode == KVX_MODE_SM || mode == KVX_MODE_SM_BULK) {
+    const bool bulk = mode == KVX_MODE_SM_BULK && local;
+    rc = run_sm(st, copies, waves, local ? Path::kDevice : Path::kPeer, bulk, s, tn);
+    mode = bulk ? KVX_MODE_SM_BULK : KVX_MODE_SM;
+  } else {
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "unknown transfer mode");
+  }
+  if (rc == KVX_OK) t_last_mode = mode;
+  return rc;
+}
+
+// ---- IPC -----------------------------------------------------------------------
+namespace {
+std::mutex g_ipc_mu;
+std::map<uint64_t, uint64_t> g_ipc_bases;  // returned pointer -> mapped base
+
+using GetRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+GetRangeFn get_range_fn() {
+  static GetRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return static_cast<GetRangeFn>(nullptr);
+    return reinterpret_cast<GetRangeFn>(p);
+  }();
+  return fn;
+}
+}  // namespace
+
+int kvx_ipc_export(void* dev_ptr, uint8_t* handle_out64, uint64_t* offset_out) {
+  t_last_error.clear();
+  if (!dev_ptr || !handle_out64 || !offset_out)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "null argument");
+  GetRangeFn fn = get_range_fn();
+  if (!fn) return set_error(KVX_ERR_CUDA, "cuMemGetAddressRange unavailable");
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  if (fn(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "pointer is not in a device allocation");
+  cudaIpcMemHandle_t h;
+  KVX_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+  std::memcpy(handle_out64, &h, 64);
+  *offset_out = reinterpret_cast<uint64_t>(dev_ptr) - uint64_t(base);
+  return KVX_OK;
+}
+
+int kvx_ipc_import(int device, const uint8_t* handle64, uint64_t offset, void** dev_ptr_out) {
+  t_last_error.clear();
+  if (!handle64 || !dev_ptr_out) return set_error(KVX_ERR_INVALID_ARGUMENT, "null argument");
+  DeviceGuard dg(device);
+  if (!dg.ok()) return set_error(KVX_ERR_CUDA, "cannot select device");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, 64);
+  void* base = nullptr;
+  KVX_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+  const uint64_t p = reinterpret_cast<uint64_t>(base) + offset;
+  {
+    std::lock_guard<std::mutex> g(g_ipc_mu);
+    g_ipc_bases[p] = reinterpret_cast<uint64_t>(base);
+  }
+  *dev_ptr_out = reinterpret_cast<void*>(p);
+  return KVX_OK;
+}
+
+int kvx_ipc_close(int device, void* dev_ptr) {
+  t_last_error.clear();
+  uint64_t base = 0;
+  {
+    std::lock_guard<std::mutex> g(g_ipc_mu);
+    auto it = g_ipc_bases.find(reinterpret_cast<uint64_t>(dev_ptr));
+    if (it == g_ipc_bases.end())
+      return set_error(KVX_ERR_INVALID_ARGUMENT, "pointer was not returned by kvx_ipc_import");
+    base = it->second;
+    g_ipc_bases.erase(it);
+  }
+  DeviceGuard dg(device);
+  KVX_CUDA(cudaIpcCloseMemHandle(reinterpret_cast<void*>(base)));
+  return KVX_OK;
+}
+
+int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,
+                       uint64_t chunk_bytes, void* stream) {
+  t_last_error.clear();
+  if (bytes && (!dst_device || !src_host))
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "null pointer");
+  if (chunk_bytes == 0) chunk_bytes = bytes ? bytes : 1;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  for (uint64_t o = 0; o < bytes; o += chunk_bytes) {
+    const uint64_t n = std::min(chunk_bytes, bytes - o);
+    KVX_CUDA(cudaMemcpyAsync(static_cast<char*>(dst_device) + o,
+                             static_cast<const char*>(src_host) + o, n,
+                             cudaMemcpyHostToDevice, s));
+  }
+  return KVX_OK;
+}
+
+int kvx_device_status(int device, int reset, int* status_out) {
+  t_last_error.clear();
+  if (!status_out) return set_error(KVX_ERR_INVALID_ARGUMENT, "null status_out");
+  DeviceGuard dg(device);
+  if (!dg.ok()) return set_error(KVX_ERR_CUDA, "cannot select device");
+  KVX_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  KVX_CUDA(cudaMemcpyFromSymbol(&v, g_kvx_device_status, sizeof(int)));
+  if (reset) {
+    const int zero = 0;
+    KVX_CUDA(cudaMemcpyToSymbol(g_kvx_device_status, &zero, sizeof(int)));
+  }
+  *status_out = v;
+  return KVX_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,218 @@
+/*
+ * kvx.h - C ABI of the B200-native KV-cache movement library (libkvx.so).
+ *
+ * The library moves paged K/V blocks between GPU HBM and page-locked host
+ * slots (swap-out / swap-in) and between two GPUs over NVLink (migration).
+ * Every entry point takes plain pointers and sizes, returns an int status
+ * (KVX_OK == 0) and is asynchronous on the CUDA stream it is given, exactly
+ * like the reference operator it replaces: it returns once the work is queued.
+ * The caller orders later work with an event on that stream.
+ *
+ * All validation happens on the host before anything is queued: an invalid
+ * request copies nothing and returns a non-zero status; kvx_last_error()
+ * then holds a one-line description for the calling thread.
+ *
+ * Reference interfaces replaced (paths inside the Aegaeon project):
+ *   kvx_swap            <- swap()                  ops/swap.cu:25-60, ops/ops.h:4-10,
+ *                                                   pybind "swap" ops/ops.cpp:4-6
+ *   kvx_layout_create   <- host view set-up         aegaeon/worker.py:1396-1433 (segments,
+ *                                                   owners, kv_swap_view) + vllm_cache.py:75-101
+ *   kvx_swap_blocks     <- Worker.swap_blocks loop  aegaeon/worker.py:2230-2329
+ *   kvx_migrate_blocks  <- Worker.migrate_blocks    aegaeon/worker.py:2420-2430 (stub in the
+ *                                                   reference: raises NotImplementedError)
+ *   kvx_ipc_export /
+ *   kvx_ipc_import      <- register_kvcache_mem_handles aegaeon/worker.py:2439-2451 (stub)
+ *   kvx_upload_chunked  <- weight upload during switch aegaeon/loader/quick_loader.py:398-444
+ *   kvx_byte_extent     <- byte_extent_for_kernel_blocks aegaeon/cache_transfer.py:138-165
+ */
+#ifndef KVX_H_
+#define KVX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define KVX_OK 0
+#define KVX_ERR_INVALID_ARGUMENT 1 /* null pointer, negative count, bad flag   */
+#define KVX_ERR_LENGTH_MISMATCH 2  /* metadata lists of different lengths     */
+#define KVX_ERR_GROUP 3            /* cache-group id outside the group table   */
+#define KVX_ERR_EXTENT 4           /* kernel-block extent invalid for the page */
+#define KVX_ERR_BLOCK_ID 5         /* block / slot id outside its buffer       */
+#define KVX_ERR_HOST_MEMORY 6      /* host buffer not usable for this mode     */
+#define KVX_ERR_CUDA 7             /* a CUDA runtime call failed               */
+#define KVX_ERR_DEVICE_TIMEOUT 8   /* a bounded device-side wait gave up       */
+#define KVX_ERR_LAYOUT 9           /* the two layouts of a migration differ    */
+#define KVX_ERR_NO_MEMORY 10       /* a library work area could not be made    */
+
+/* ---- transfer modes (the `mode` argument of the copy entry points) ------- */
+#define KVX_MODE_AUTO 0     /* per-call choice by size and fragmentation       */
+#define KVX_MODE_SM 1       /* SM kernel, 16-byte vector loads/stores; host    */
+                            /* side through its device-mapped address          */
+#define KVX_MODE_CE 2       /* copy engines over coalesced runs; HBM side      */
+                            /* gathered into / scattered from a staging area   */
+#define KVX_MODE_SM_BULK 3  /* device<->device only: TMA bulk copies through   */
+                            /* shared memory                                   */
+#define KVX_MODE_CE_EXTENT 4 /* one copy-engine copy per coalesced extent, no */
+                            /* staging (fast when extents are already large)   */
+
+const char* kvx_status_string(int status);
+/* Detail message of the last failing call made by this thread ("" if none). */
+const char* kvx_last_error(void);
+int kvx_version(void);
+
+/* ---- a1: drop-in for the reference's swap op ------------------------------
+ * For i in [0, num_ids): copy `block_bytes` bytes
+ *   swap-in : kv_swap [source_block_ids[i]] -> kv_cache[target_block_ids[i]]
+ *   swap-out: kv_cache[source_block_ids[i]] -> kv_swap [target_block_ids[i]]
+ * where buffer[id] is the byte range [id*block_bytes, (id+1)*block_bytes).
+ * kv_cache is device memory of the current device; kv_swap is host memory
+ * (page-locked for the SM path; any host memory for the copy-engine path).
+ * The reference derives block_bytes as kv_cache.numel()*2/kv_cache.size(0)
+ * (ops/swap.cu:34); callers pass that value.  When a target id repeats, the
+ * last occurrence wins, as with the reference's in-order copies.
+ * Replaces: swap() ops/swap.cu:25-60.                                        */
+int kvx_swap(const int64_t* source_block_ids, const int64_t* target_block_ids,
+             int64_t num_ids, int is_swap_in, void* kv_cache,
+             uint64_t kv_cache_bytes, uint64_t block_bytes, void* kv_swap,
+             uint64_t kv_swap_bytes, int mode, void* stream);
+
+/* ---- a2/a7/a8: segmented multi-layer layout -------------------------------
+ * A layout describes, for one GPU, the backing tensors ("segments") of a
+ * composite KV block and the host pool that holds swapped blocks:
+ *   segment s: device pages at segment_pages[s] (block id b at
+ *              b*segment_page_bytes[s]), segment_num_blocks[s] pages;
+ *              cpu_offset = byte offset of this segment inside one host row;
+ *              owner mask = bit g set when cache group g may copy it.
+ *   group g  : group_blocks_per_kv_block[g] kernel blocks per physical block.
+ *   host pool: host_pool bytes, row r at r*host_row_bytes; the bytes of this
+ *              GPU start at host_row_offset inside each row (tp_rank times the
+ *              composite page in the reference).
+ * host_pool may be NULL for a layout used only as a migration endpoint.
+ * The layout copies the tables, not the memory they point to.
+ * Replaces: worker.py:1396-1433 (owners, kv_swap_view), vllm_cache.py:75-101. */
+typedef struct kvx_layout kvx_layout;
+
+int kvx_layout_create(int device, int64_t num_segments,
+                      void* const* segment_pages,
+                      const uint64_t* segment_page_bytes,
+                      const uint64_t* segment_num_blocks,
+                      const uint64_t* segment_cpu_offsets,
+                      const uint64_t* segment_owner_masks, int64_t num_groups,
+                      const int64_t* group_blocks_per_kv_block, void* host_pool,
+                      uint64_t host_pool_bytes, uint64_t host_row_bytes,
+                      uint64_t host_row_offset, kvx_layout** layout_out);
+int kvx_layout_destroy(kvx_layout* layout);
+
+/* Swap the live extents of entries between GPU pages and host rows.
+ * Entry i: block source_block_ids[i] -> target_block_ids[i] (GPU page id and
+ * host row id, by direction), owned by cache group group_ids[i], live extent =
+ * kernel blocks [first_kernel_blocks[i], first+valid_kernel_blocks[i]) of the
+ * page.  For every segment owned by the group the byte extent
+ *   (page/ratio*first, page/ratio*valid)
+ * is copied; zero-length extents are skipped.  copied_bytes / copy_extents
+ * (optional, may be NULL) report the totals the reference logs.
+ * Replaces: Worker.swap_blocks hot loop, worker.py:2230-2329.               */
+int kvx_swap_blocks(kvx_layout* layout, int64_t num_entries,
+                    const int64_t* source_block_ids,
+                    const int64_t* target_block_ids, const int64_t* group_ids,
+                    const int64_t* first_kernel_blocks,
+                    const int64_t* valid_kernel_blocks, int is_swap_in, int mode,
+                    void* stream, uint64_t* copied_bytes,
+                    uint64_t* copy_extents);
+
+/* ---- a10: GPU -> GPU migration over NVLink ---------------------------------
+ * Same entry semantics as kvx_swap_blocks, with source pages in `source` and
+ * target pages in `target`.  The copy runs on the SMs of the current device,
+ * which must be able to address both layouts' pages: its own memory, and a
+ * peer's memory mapped into this process with kvx_ipc_import.  Pull (run on
+ * the target GPU, source pages imported) and push (run on the source GPU,
+ * target pages imported) are both valid; each 16-byte load or store that
+ * crosses NVLink is a plain peer access (no multicast).  The segment tables
+ * of the two layouts must agree in count, page sizes and owners, and their
+ * group tables must be equal.
+ * Fills: Worker.migrate_blocks, worker.py:2420-2430 (NotImplementedError in
+ * the reference; its prefill->decode route is swap-out then swap-in).       */
+int kvx_migrate_blocks(kvx_layout* source, kvx_layout* target,
+                       int64_t num_entries, const int64_t* source_block_ids,
+                       const int64_t* target_block_ids,
+                       const int64_t* group_ids,
+                       const int64_t* first_kernel_blocks,
+                       const int64_t* valid_kernel_blocks, int mode,
+                       void* stream, uint64_t* copied_bytes,
+                       uint64_t* copy_extents);
+
+/* ---- IPC memory handles (peer mapping of a KV cache) -----------------------
+ * export: 64-byte handle of the allocation holding dev_ptr, plus the offset
+ * of dev_ptr inside that allocation.  import: maps the allocation (peer access
+ * enabled lazily) and returns base+offset.  close: unmaps a pointer returned by
+ * import.  Fills: register/unregister_kvcache_mem_handles, worker.py:2439-2451. */
+int kvx_ipc_export(void* dev_ptr, uint8_t* handle_out64, uint64_t* offset_out);
+int kvx_ipc_import(int device, const uint8_t* handle64, uint64_t offset,
+                   void** dev_ptr_out);
+int kvx_ipc_close(int device, void* dev_ptr);
+
+/* ---- (f1) chunked weight upload for a model switch --------------------------
+ * Host -> device copy of `bytes` bytes issued as copy-engine copies of at most
+ * chunk_bytes each on `stream` (64 MiB chunks in the switch pipeline).
+ * Replaces: the slice_storage.copy_(non_blocking=True) loop,
+ * aegaeon/loader/quick_loader.py:398-444.                                    */
+int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,
+                       uint64_t chunk_bytes, void* stream);
+
+/* ---- a3: extent arithmetic (host only, no GPU needed) ---------------------
+ * (first, count) kernel blocks of a page of page_bytes split into
+ * kernel_blocks_per_page -> (byte_offset, byte_length).  Same checks and
+ * results as byte_extent_for_kernel_blocks, cache_transfer.py:138-165.      */
+int kvx_byte_extent(uint64_t page_bytes, int64_t kernel_blocks_per_page,
+                    int64_t first_kernel_block, int64_t num_kernel_blocks,
+                    uint64_t* byte_offset_out, uint64_t* byte_length_out);
+
+/* ---- planning introspection (host only, no GPU needed) ---------------------
+ * Run the validation and planning of kvx_swap_blocks / kvx_swap without
+ * touching a GPU and return the copies it would issue, in issue order, as
+ * (source address, destination address, bytes) triples.  *num_copies_inout
+ * holds the capacity of the three arrays on entry and the number of copies on
+ * return (when the capacity is too small the arrays are left unfilled and
+ * KVX_OK is returned with the required count).  Used by tests of the host
+ * logic and by callers that want to inspect a plan.                          */
+int kvx_plan_swap_blocks(const kvx_layout* layout, int64_t num_entries,
+                         const int64_t* source_block_ids,
+                         const int64_t* target_block_ids,
+                         const int64_t* group_ids,
+                         const int64_t* first_kernel_blocks,
+                         const int64_t* valid_kernel_blocks, int is_swap_in,
+                         uint64_t* src_addrs, uint64_t* dst_addrs,
+                         uint64_t* lengths, int64_t* num_copies_inout);
+int kvx_plan_swap(const int64_t* source_block_ids,
+                  const int64_t* target_block_ids, int64_t num_ids,
+                  int is_swap_in, uint64_t kv_cache, uint64_t kv_cache_bytes,
+                  uint64_t block_bytes, uint64_t kv_swap,
+                  uint64_t kv_swap_bytes, uint64_t* src_addrs,
+                  uint64_t* dst_addrs, uint64_t* lengths,
+                  int64_t* num_copies_inout);
+
+/* ---- statistics and device status ------------------------------------------
+ * kvx_last_mode: the transfer mode the last successful copy call of this
+ * thread used (KVX_MODE_SM / _CE / _SM_BULK / _CE_EXTENT).
+ * kvx_device_status: reads (and with reset != 0 clears) the device error word
+ * written by kernels whose bounded waits gave up; synchronizes the device.  */
+int kvx_last_mode(void);
+int kvx_device_status(int device, int reset, int* status_out);
+
+/* Tuning knobs of KVX_MODE_AUTO and of the kernels; 0 keeps the current value.
+ *   sm_ctas_host : CTAs of an SM kernel that touches host memory
+ *   sm_ctas_dev  : CTAs of an SM kernel that touches device memory only
+ *   ce_min_run   : mean coalesced host-run bytes from which AUTO uses the CE
+ *   staging_bytes: size of each staging area of the copy-engine mode        */
+int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
+                  int64_t ce_min_run, int64_t staging_bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVX_H_ */

@@ -1,0 +1,303 @@
+"""Generate golden fixtures by running the reference's own Python code.
+
+Run in a container that has the Aegaeon checkout (default /root/reference,
+override with AEGAEON_REFERENCE); the fixtures it writes are committed and the
+tests never read the checkout.  Nothing is written into the checkout (the
+reference logger writes ``output.log`` into the working directory, so this
+script runs from a temporary one).
+
+Fixtures:
+  extents.json       cache_transfer.py helpers over a grid of arguments
+                     (results, or exception type + message)
+  block_tables.json  BlockTable.transfer_entries / moved_group_blocks /
+                     swap_metadata and CacheGroupRuntimeConfig extents from
+                     block_manager.py (``ray`` stubbed; it is not used there)
+  swap_blocks.json   Worker.swap_blocks (worker.py:2204-2349), extracted from
+                     the source with ``ast`` and executed on CPU tensors with
+                     CUDA streams/events stubbed, on seeded byte contents:
+                     the resulting host pool and GPU pages (hex) per step.
+
+Usage:  python tests/golden/make_golden.py
+"""
+
+from __future__ import annotations
+
+import ast
+import contextlib
+import hashlib
+import json
+import os
+import sys
+import tempfile
+import types
+
+import numpy as np
+
+REF = os.environ.get("AEGAEON_REFERENCE", "/root/reference")
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def stub_ray() -> None:
+    ray = types.ModuleType("ray")
+    ray.ObjectRef = object
+    ray.remote = lambda *a, **k: (lambda f: f)
+    ray.get = lambda x: x
+    actor = types.ModuleType("ray.actor")
+    actor.exit_actor = lambda: None
+    ray.actor = actor
+    sys.modules.setdefault("ray", ray)
+    sys.modules.setdefault("ray.actor", actor)
+
+
+def outcome(fn, *args):
+    try:
+        r = fn(*args)
+        if isinstance(r, tuple):
+            r = list(r)
+        return {"ok": r}
+    except Exception as e:  # noqa: BLE001 - the exception is the recorded result
+        return {"error": type(e).__name__, "message": str(e)}
+
+
+def gen_extents(ct) -> dict:
+    cases = {k: [] for k in (
+        "logical_blocks_for_tokens", "sliding_window_resident_block_bound",
+        "num_skipped_sliding_window_blocks", "kernel_block_extent_for_attention_page",
+        "prefix_bytes_for_kernel_blocks", "byte_extent_for_kernel_blocks")}
+    for n in (-1, 0, 1, 15, 16, 17, 255, 256, 257, 1057):
+        for bs in (-1, 0, 1, 16, 528):
+            cases["logical_blocks_for_tokens"].append(
+                [[n, bs], outcome(ct.logical_blocks_for_tokens, n, bs)])
+            for w in (-3, 0, 1, 2, 16, 17, 100, 4096):
+                cases["sliding_window_resident_block_bound"].append(
+                    [[n, bs, w], outcome(ct.sliding_window_resident_block_bound, n, bs, w)])
+                cases["num_skipped_sliding_window_blocks"].append(
+                    [[n, bs, w], outcome(ct.num_skipped_sliding_window_blocks, n, bs, w)])
+    for cached in (-1, 0, 15, 17, 100, 528, 529, 1057):
+        for idx in (-1, 0, 1, 3):
+            for pbs, kbs in ((16, 16), (528, 16), (64, 16), (48, 32), (0, 16)):
+                for w in (None, -1, 1, 17, 600):
+                    cases["kernel_block_extent_for_attention_page"].append(
+                        [[cached, idx, pbs, kbs, w],
+                         outcome(ct.kernel_block_extent_for_attention_page, cached, idx, pbs,
+                                 kbs, w)])
+    for page in (-16, 0, 17, 65536, 17301504 // 8):
+        for ratio in (-1, 0, 1, 4, 33):
+            for valid in (-1, 0, 1, 4, 34):
+                cases["prefix_bytes_for_kernel_blocks"].append(
+                    [[page, ratio, valid], outcome(ct.prefix_bytes_for_kernel_blocks, page,
+                                                   ratio, valid)])
+                for first in (-1, 0, 3):
+                    cases["byte_extent_for_kernel_blocks"].append(
+                        [[page, ratio, first, valid],
+                         outcome(ct.byte_extent_for_kernel_blocks, page, ratio, first, valid)])
+    return cases
+
+
+def gen_block_tables(bm) -> dict:
+    rng = np.random.default_rng(7)
+    out = {"runtime_extents": [], "tables": []}
+    for kind, kvb, kb, w in (("attention", 16, 16, None), ("attention", 528, 16, None),
+                             ("attention", 64, 16, 40), ("mamba_none", 1, 1, None)):
+        cfg = bm.CacheGroupRuntimeConfig(kind, kvb, kb, w)
+        for page in (16, 4096, 17301504 // 8, 65536):
+            for first in range(0, cfg.blocks_per_kv_block + 1, max(1, cfg.blocks_per_kv_block // 3)):
+                for num in (0, 1, cfg.blocks_per_kv_block - first, cfg.blocks_per_kv_block + 1):
+                    out["runtime_extents"].append(
+                        [[kind, kvb, kb, w, page, first, num],
+                         outcome(cfg.byte_extent_for_kernel_blocks, page, first, num)])
+        out.setdefault("to_kernel_ids", []).append(
+            [[kind, kvb, kb, w], cfg.to_kernel_block_ids([3, -1, 0, 7])])
+    group_sets = [
+        [("attention", 16, 16, None)],
+        [("attention", 528, 16, None), ("mamba_none", 528, 528, None)],
+        [("attention", 64, 16, 40), ("attention", 16, 16, None)],
+        [("attention", 32, 16, 1)],
+    ]
+    for gs in group_sets:
+        groups = tuple(bm.CacheGroupConfig(*g) for g in gs)
+        for processed in (0, 1, 15, 16, 17, 63, 64, 65, 200, 529, 1100):
+            blocks = []
+            for g in groups:
+                n = g.table_blocks_for_tokens(max(processed, 1))
+                ids = [int(x) for x in rng.choice(10000, size=n, replace=False)]
+                if g.sliding_window is not None and n > 2:
+                    ids[0] = bm.LOGICAL_NULL_BLOCK_ID
+                blocks.append(ids)
+            bt = bm.BlockTable(0, (1,), groups, [list(b) for b in blocks])
+            entries = bt.transfer_entries(processed)
+            targets = [int(x) for x in rng.choice(10000, size=len(entries), replace=False)]
+            rec = {
+                "groups": gs, "processed": processed, "group_blocks": blocks,
+                "transfer_entries": [list(e) for e in entries],
+                "targets": targets,
+                "moved": bt.moved_group_blocks(processed, targets),
+                "swap_metadata": [list(x) for x in bt.swap_metadata(processed)],
+                "blocks": bt.blocks,
+            }
+            bt2 = bm.BlockTable(0, (1,), groups, [list(b) for b in blocks])
+            rec["released"] = bt2.release_skipped_blocks(processed)
+            rec["after_release"] = bt2.group_blocks
+            out["tables"].append(rec)
+    return out
+
+
+def load_swap_blocks(bm):
+    """Worker.swap_blocks from worker.py, runnable on CPU tensors."""
+    import torch
+
+    src = open(os.path.join(REF, "aegaeon", "worker.py")).read()
+    tree = ast.parse(src)
+    cls = next(n for n in tree.body if isinstance(n, ast.ClassDef) and n.name == "Worker")
+    fn = next(n for n in cls.body if isinstance(n, ast.FunctionDef) and n.name == "swap_blocks")
+    fn.decorator_list = []
+    code = compile(ast.Module(body=[fn], type_ignores=[]), "worker.py", "exec")
+
+    class FakeEvent:
+        def __init__(self, *a, **k):
+            pass
+
+        def record(self, *a, **k):
+            pass
+
+    fake_cuda = types.SimpleNamespace(Event=FakeEvent, stream=lambda s: contextlib.nullcontext())
+
+    class TorchProxy(types.ModuleType):
+        def __getattr__(self, name):
+            if name == "cuda":
+                return fake_cuda
+            return getattr(torch, name)
+
+    class Logger:
+        def info(self, *a, **k):
+            pass
+
+        debug = error = warning = info
+
+    ray = sys.modules["ray"]
+    ns = {"torch": TorchProxy("torch"), "ray": ray, "cudaStream_t": lambda x: x,
+          "reduce_cuda_event": lambda *a: None, "logger": Logger()}
+    exec(code, ns)
+    return ns["swap_blocks"]
+
+
+def gen_swap_blocks(bm) -> dict:
+    import torch
+
+    swap_blocks = load_swap_blocks(bm)
+    scenarios = []
+    specs = [
+        # name, segment page bytes, owners, groups (kind, kv, kernel), gpu blocks,
+        # host rows, tp (rank, size)
+        ("hybrid", [64, 128, 64, 256], [[0], [0, 1], [1], [0]],
+         [("attention", 64, 16), ("mamba_none", 16, 16)], 12, 10, (1, 2)),
+        ("uniform", [96, 96, 96], [[0], [0], [0]], [("attention", 16, 16)], 9, 8, (0, 1)),
+        ("ragged", [24, 48, 24], [[0], [0, 1], [1]], [("attention", 24, 8), ("mamba_none", 8, 8)],
+         7, 6, (0, 1)),
+    ]
+    for name, pages, owners, groups, nblocks, nrows, (tp_rank, tp_size) in specs:
+        rng = np.random.default_rng(11 + len(scenarios))
+        descs = [bm.CacheGroupRuntimeConfig(k, kv, kb) for k, kv, kb in groups]
+        composite = sum(pages)
+        offsets = list(np.cumsum([0] + pages[:-1]))
+        seg_init = [rng.integers(0, 256, size=nblocks * p, dtype=np.uint8) for p in pages]
+        pool_init = rng.integers(0, 256, size=nrows * composite * tp_size, dtype=np.uint8)
+        raw = {f"seg{i}": torch.from_numpy(seg_init[i].copy()).view(torch.int8)
+               for i in range(len(pages))}
+        pool = torch.from_numpy(pool_init.copy())
+        view = pool.view(nrows, composite * tp_size)
+        segs = [types.SimpleNamespace(layer_name=f"seg{i}", cpu_offset=int(offsets[i]),
+                                      page_size_bytes=p) for i, p in enumerate(pages)]
+        self = types.SimpleNamespace(
+            cache_group_descriptors=descs,
+            swap_in_stream=types.SimpleNamespace(cuda_stream=0),
+            swap_out_stream=types.SimpleNamespace(cuda_stream=0),
+            _wait_source_events=lambda *a, **k: None,
+            composite_cache=types.SimpleNamespace(page_size_bytes=composite, segments=segs,
+                                                  raw_tensors=raw),
+            cache_segment_group_ids=[frozenset(o) for o in owners],
+            parallel_config=types.SimpleNamespace(tensor_parallel_rank=tp_rank),
+            kv_swap_view=view, cudart=None)
+        steps = []
+        for step in range(3):
+            is_in = step == 1
+            n = int(rng.integers(3, 7))
+            dev_ids = [int(x) for x in rng.choice(nblocks, size=n, replace=False)]
+            rows = [int(x) for x in rng.choice(nrows, size=n, replace=False)]
+            gids, firsts, valids = [], [], []
+            for _ in range(n):
+                g = int(rng.integers(0, len(descs)))
+                r = descs[g].blocks_per_kv_block
+                f = int(rng.integers(0, r))
+                v = int(rng.integers(0, r - f + 1))
+                if step == 2:
+                    f, v = 0, r
+                gids.append(g)
+                firsts.append(f)
+                valids.append(v)
+            srcs, dsts = (rows, dev_ids) if is_in else (dev_ids, rows)
+            swap_blocks(self, list(range(n)), srcs, dsts, gids, firsts, valids, [None] * n, is_in)
+            steps.append({
+                "is_swap_in": is_in, "source": srcs, "target": dsts, "groups": gids,
+                "first": firsts, "valid": valids,
+                "pool_sha256": hashlib.sha256(pool.numpy().tobytes()).hexdigest(),
+                "segments_sha256": [
+                    hashlib.sha256(raw[f"seg{i}"].view(torch.uint8).numpy().tobytes()).hexdigest()
+                    for i in range(len(pages))],
+            })
+        steps[-1]["pool"] = pool.numpy().tobytes().hex()
+        steps[-1]["segments"] = [raw[f"seg{i}"].view(torch.uint8).numpy().tobytes().hex()
+                                 for i in range(len(pages))]
+        errors = []
+        for label, args in (
+            ("bad_group", ([0], [0], [len(descs)], [0], [1], False)),
+            ("bad_extent", ([0], [0], [0], [descs[0].blocks_per_kv_block], [1], False)),
+            ("bad_row", ([0], [nrows], [0], [0], [1], False)),
+            ("bad_lengths", ([0, 1], [0], [0], [0], [1], False)),
+        ):
+            s_, d_, g_, f_, v_, inn = args
+            errors.append([label, list(args),
+                           outcome(swap_blocks, self, [0] * len(s_), s_, d_, g_, f_, v_,
+                                   [None] * len(s_), inn)])
+        scenarios.append({
+            "name": name, "pages": pages, "owners": owners, "groups": groups,
+            "num_blocks": nblocks, "num_rows": nrows, "tp_rank": tp_rank, "tp_size": tp_size,
+            "cpu_offsets": [int(x) for x in offsets],
+            "init_segments": [a.tobytes().hex() for a in seg_init],
+            "init_pool": pool_init.tobytes().hex(), "steps": steps, "errors": errors,
+        })
+    return {"scenarios": scenarios}
+
+
+def main() -> None:
+    if not os.path.isdir(os.path.join(REF, "aegaeon")):
+        sys.exit(f"reference checkout not found at {REF}")
+    sys.path.insert(0, REF)
+    stub_ray()
+    cwd = os.getcwd()
+    with tempfile.TemporaryDirectory() as tmp:
+        os.chdir(tmp)
+        try:
+            import aegaeon.block_manager as bm
+            import aegaeon.cache_transfer as ct
+
+            fixtures = {
+                "extents.json": gen_extents(ct),
+                "block_tables.json": gen_block_tables(bm),
+                "swap_blocks.json": gen_swap_blocks(bm),
+            }
+        finally:
+            os.chdir(cwd)
+    for name, data in fixtures.items():
+        with open(os.path.join(OUT, name), "w") as f:
+            json.dump({"generator": "tests/golden/make_golden.py",
+                       "reference_files": {
+                           "extents.json": "aegaeon/cache_transfer.py",
+                           "block_tables.json": "aegaeon/block_manager.py",
+                           "swap_blocks.json": "aegaeon/worker.py (Worker.swap_blocks)"}[name],
+                       "data": data}, f, separators=(",", ":"))
+        print(name, os.path.getsize(os.path.join(OUT, name)), "bytes")
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,154 @@
+"""GPU->GPU block migration (the reference's unimplemented migrate_blocks,
+worker.py:2420-2451): same-GPU copies through both kernels, and, with two
+GPUs, pull and push over IPC-mapped peer memory."""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from aegaeon_b200 import _lib, swapper
+
+pytestmark = pytest.mark.gpu
+
+
+def cache_pages(device, layers, blocks, page, seed):
+    g = torch.Generator(device=device).manual_seed(seed)
+    return [torch.randint(0, 255, (blocks * page,), generator=g, dtype=torch.uint8,
+                          device=device) for _ in range(layers)]
+
+
+def make(device, pages_per_seg, seg_tensors):
+    segments, _ = swapper.make_segments(
+        [((f"l{i}",), t.numel()) for i, t in enumerate(seg_tensors)],
+        seg_tensors[0].numel() // pages_per_seg)
+    return swapper.KVSwapper(device, segments, seg_tensors, [frozenset({0})] * len(seg_tensors), [1])
+
+
+def expected_after(src_pages, dst_pages, src_ids, dst_ids, page):
+    exp = [d.cpu().numpy().copy() for d in dst_pages]
+    for s, d in zip(src_pages, exp):
+        sv = s.cpu().numpy()
+        for a, b in zip(src_ids, dst_ids):
+            d[b * page:(b + 1) * page] = sv[a * page:(a + 1) * page]
+    return exp
+
+
+@pytest.mark.parametrize("mode", ["sm", "sm_bulk", "ce"])
+def test_same_gpu_migration(cuda, mode):
+    page, blocks, layers = 16384, 256, 6
+    src = cache_pages(cuda, layers, blocks, page, 1)
+    dst = cache_pages(cuda, layers, blocks, page, 2)
+    a, b = make(0, page, src), make(0, page, dst)
+    g = torch.Generator().manual_seed(3)
+    sid = torch.randperm(blocks, generator=g)[:150].tolist()
+    did = torch.randperm(blocks, generator=g)[:150].tolist()
+    exp = expected_after(src, dst, sid, did, page)
+    n = len(sid)
+    s_ep, t_ep = a.local_endpoint(), b.local_endpoint()
+    stream = torch.cuda.current_stream()
+    import ctypes
+    arr = swapper._entry_arrays(sid, did, [0] * n, [0] * n, [1] * n)
+    _lib.check(_lib.lib().kvx_migrate_blocks(s_ep.handle, t_ep.handle, *arr, _lib.mode_of(mode),
+                                             stream.cuda_stream, None, None))
+    torch.cuda.synchronize()
+    assert _lib.last_mode_name() == {"ce": "ce_extent"}.get(mode, mode)
+    for d, e in zip(dst, exp):
+        assert np.array_equal(d.cpu().numpy(), e)
+    assert _lib.device_status(0) == 0
+    a.close()
+    b.close()
+
+
+@pytest.mark.parametrize("mode", ["sm", "sm_bulk"])
+def test_copy_blocks_local_overlapping_ids(cuda, mode):
+    """Source and target ids overlap inside one cache: bytes equal a
+    sequential in-order loop (the planner splits conflicting copies into
+    ordered waves)."""
+    page, blocks = 32768, 16
+    pages = cache_pages(cuda, 2, blocks, page, 4)
+    sw = make(0, page, pages)
+    src_ids, dst_ids = [0, 1, 2, 3, 4], [1, 2, 3, 4, 5]
+    exp = [p.cpu().numpy().copy() for p in pages]
+    for e in exp:
+        for a, b in zip(src_ids, dst_ids):
+            e[b * page:(b + 1) * page] = e[a * page:(a + 1) * page]
+    sw.copy_blocks_local(src_ids, dst_ids, mode=mode).synchronize()
+    for p, e in zip(pages, exp):
+        assert np.array_equal(p.cpu().numpy(), e)
+    sw.close()
+
+
+def _peer_worker(rank, world, q_out, q_in, page, blocks, layers, direction):
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    pages = cache_pages(dev, layers, blocks, page, 100 + rank)
+    sw = make(rank, page, pages)
+    g = torch.Generator().manual_seed(5)
+    sid = torch.randperm(blocks, generator=g)[:200].tolist()
+    did = torch.randperm(blocks, generator=g)[:200].tolist()
+    q_out.put(("handles", rank, sw.export_kvcache_mem_handles()))
+    _, peer, handles = q_in.get(timeout=120)
+    torch.cuda.synchronize()
+    if rank == 1:  # the decode side: register prefill's cache and pull
+        sw.register_kvcache_mem_handles(0, None, handles)
+        src_snapshot = None
+        if direction == "pull":
+            ev = sw.migrate_blocks([1], 0, sid, did, [None], direction="pull")
+            ev.synchronize()
+        q_out.put(("done", rank, None))
+    else:
+        sw.register_kvcache_mem_handles(1, None, handles)
+        if direction == "push":
+            sw.migrate_blocks([1], 1, sid, did, [None], direction="push").synchronize()
+        q_out.put(("done", rank, None))
+    q_in.get(timeout=120)  # both finished
+    out = [p.cpu().numpy().tobytes() for p in pages] if rank == 1 else None
+    q_out.put(("pages", rank, out))
+    q_in.get(timeout=120)
+    sw.close()
+
+
+@pytest.mark.multigpu
+@pytest.mark.parametrize("direction", ["pull", "push"])
+def test_two_gpu_migration(cuda, direction):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    page, blocks, layers = 16384, 512, 4
+    q0, q1, qa, qb = ctx.Queue(), ctx.Queue(), ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_peer_worker, args=(0, 2, q0, qa, page, blocks, layers, direction)),
+             ctx.Process(target=_peer_worker, args=(1, 2, q1, qb, page, blocks, layers, direction))]
+    for p in procs:
+        p.start()
+    try:
+        h0 = q0.get(timeout=180)
+        h1 = q1.get(timeout=180)
+        qa.put(h1)
+        qb.put(h0)
+        assert q0.get(timeout=180)[0] == "done"
+        assert q1.get(timeout=180)[0] == "done"
+        qa.put("go")
+        qb.put("go")
+        q0.get(timeout=180)
+        got = q1.get(timeout=180)[2]
+        qa.put("end")
+        qb.put("end")
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    # expected: rank 1's pages with rank 0's selected blocks copied in
+    src = cache_pages(torch.device("cuda", 0), layers, blocks, page, 100)
+    dst = cache_pages(torch.device("cuda", 1), layers, blocks, page, 101)
+    g = torch.Generator().manual_seed(5)
+    sid = torch.randperm(blocks, generator=g)[:200].tolist()
+    did = torch.randperm(blocks, generator=g)[:200].tolist()
+    exp = expected_after(src, dst, sid, did, page)
+    for e, b in zip(exp, got):
+        assert e.tobytes() == b
+    assert all(p.exitcode == 0 for p in procs)
