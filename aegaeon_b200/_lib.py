@@ -80,6 +80,9 @@ SIGNATURES = {
         [_p_i64, _p_i64, _i64, _int, _u64, _u64, _u64, _u64, _u64, _p_u64, _p_u64, _p_u64, _p_i64],
     ),
     "kvx_last_mode": (_int, []),
+    "kvx_kernel_launches": (_u64, []),
+    "kvx_kernel_timing": (_int, [_int]),
+    "kvx_kernel_timing_read": (_int, [_p_u64, ctypes.POINTER(ctypes.c_double), _p_u64]),
     "kvx_device_status": (_int, [_int, _int, ctypes.POINTER(_int)]),
     "kvx_configure": (_int, [_i64, _i64, _i64, _i64]),
 }
@@ -176,3 +179,17 @@ def device_status(device: int, reset: bool = False) -> int:
     out = ctypes.c_int(0)
     check(lib().kvx_device_status(device, 1 if reset else 0, ctypes.byref(out)))
     return out.value
+
+
+def kernel_timing(enable: bool) -> None:
+    """Bracket every copy-kernel launch with CUDA events (see kvx.h)."""
+    check(lib().kvx_kernel_timing(1 if enable else 0))
+
+
+def kernel_timing_read() -> tuple[int, float, int]:
+    """(launches, summed kernel milliseconds, HBM bytes) since the last read."""
+    n = ctypes.c_uint64()
+    ms = ctypes.c_double()
+    b = ctypes.c_uint64()
+    check(lib().kvx_kernel_timing_read(ctypes.byref(n), ctypes.byref(ms), ctypes.byref(b)))
+    return n.value, ms.value, b.value

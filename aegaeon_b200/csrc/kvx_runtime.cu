@@ -15,6 +15,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -34,6 +35,18 @@ namespace {
 
 thread_local std::string t_last_error;
 thread_local int t_last_mode = 0;
+std::atomic<uint64_t> g_kernel_launches{0};
+
+// Optional per-launch timing: an event pair around every copy kernel, read
+// back by kvx_kernel_timing_read.  Off unless a caller enables it.
+struct TimedLaunch {
+  int device;
+  cudaEvent_t begin, end;
+  uint64_t hbm_bytes;
+};
+std::atomic<bool> g_timing{false};
+std::mutex g_timing_mu;
+std::vector<TimedLaunch> g_timed;
 
 int set_error(int code, const std::string& msg) {
   t_last_error = msg;
@@ -61,7 +74,7 @@ int from_plan(const Error& e) {
 struct Tunables {
   int64_t sm_ctas_host = 0;    // 0: number of SMs
   int64_t sm_ctas_dev = 0;     // 0: 8 x number of SMs
-  int64_t ce_min_run = 8ll << 20;
+  int64_t ce_min_run = 1ll << 20;
   int64_t staging_bytes = 256ll << 20;
 };
 std::mutex g_tun_mu;
@@ -276,7 +289,20 @@ struct Launch {
   uint32_t n_tiles;
   bool bulk;
   Path path;
+  uint64_t bytes;    // payload bytes of this launch
 };
+
+// HBM bytes a launch moves on this GPU: read + write when both sides are
+// local, one side when the other is host or peer memory.
+uint64_t hbm_bytes_of(const Launch& l) {
+  return l.path == Path::kDevice ? 2 * l.bytes : l.bytes;
+}
+
+uint64_t payload_of(const std::vector<Copy>& v) {
+  uint64_t b = 0;
+  for (const Copy& c : v) b += c.len;
+  return b;
+}
 
 int upload_items(DeviceState* st, const std::vector<Item>& items,
                  cudaStream_t s, size_t* ring_off) {
@@ -300,9 +326,26 @@ int ensure_bulk(DeviceState* st) {
   return KVX_OK;
 }
 
+int launch_kernel(DeviceState* st, const Item* dev_items, const Launch& l,
+                  cudaStream_t s, const Tunables& tn);
+
 int launch_one(DeviceState* st, const Item* dev_items, const Launch& l,
                cudaStream_t s, const Tunables& tn) {
   if (l.n_tiles == 0) return KVX_OK;
+  if (!g_timing.load(std::memory_order_relaxed)) return launch_kernel(st, dev_items, l, s, tn);
+  TimedLaunch t{st->device, nullptr, nullptr, hbm_bytes_of(l)};
+  KVX_CUDA(cudaEventCreate(&t.begin));
+  KVX_CUDA(cudaEventCreate(&t.end));
+  KVX_CUDA(cudaEventRecord(t.begin, s));
+  int rc = launch_kernel(st, dev_items, l, s, tn);
+  KVX_CUDA(cudaEventRecord(t.end, s));
+  std::lock_guard<std::mutex> g(g_timing_mu);
+  g_timed.push_back(t);
+  return rc;
+}
+
+int launch_kernel(DeviceState* st, const Item* dev_items, const Launch& l,
+                  cudaStream_t s, const Tunables& tn) {
   if (l.bulk) {
     int rc = ensure_bulk(st);
     if (rc) return rc;
@@ -320,6 +363,7 @@ int launch_one(DeviceState* st, const Item* dev_items, const Launch& l,
                                                             l.n_tiles, 15);
   }
   KVX_CUDA(cudaGetLastError());
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
   return KVX_OK;
 }
 
@@ -342,7 +386,8 @@ int run_sm(DeviceState* st, const std::vector<Copy>& copies,
     const uint64_t tiles = build_items(w, bulk ? kBulkChunk : kVecTile, &tmp);
     if (tiles > 0xffffffffull)
       return set_error(KVX_ERR_INVALID_ARGUMENT, "request too large for one launch");
-    launches.push_back(Launch{all.size(), uint32_t(tmp.size()), uint32_t(tiles), bulk, path});
+    launches.push_back(Launch{all.size(), uint32_t(tmp.size()), uint32_t(tiles), bulk, path,
+                              payload_of(w)});
     all.insert(all.end(), tmp.begin(), tmp.end());
   }
   size_t off = 0;
@@ -384,7 +429,7 @@ int run_ce_staged(DeviceState* st, const std::vector<Copy>& copies,
       const bool bulk = allow_bulk && all_aligned16(ch.device_moves);
       const uint64_t tiles = build_items(ch.device_moves, bulk ? kBulkChunk : kVecTile, &tmp);
       launches.push_back(Launch{all.size(), uint32_t(tmp.size()), uint32_t(tiles), bulk,
-                                Path::kDevice});
+                                Path::kDevice, payload_of(ch.device_moves)});
       all.insert(all.end(), tmp.begin(), tmp.end());
     }
     plans.push_back(std::move(chunks));
@@ -544,6 +589,39 @@ const char* kvx_status_string(int status) {
 const char* kvx_last_error(void) { return t_last_error.c_str(); }
 int kvx_version(void) { return 10000; }
 int kvx_last_mode(void) { return t_last_mode; }
+uint64_t kvx_kernel_launches(void) { return g_kernel_launches.load(); }
+
+int kvx_kernel_timing(int enable) {
+  g_timing.store(enable != 0);
+  return KVX_OK;
+}
+
+int kvx_kernel_timing_read(uint64_t* launches, double* total_ms, uint64_t* hbm_bytes) {
+  t_last_error.clear();
+  std::vector<TimedLaunch> v;
+  {
+    std::lock_guard<std::mutex> g(g_timing_mu);
+    v.swap(g_timed);
+  }
+  uint64_t n = 0, bytes = 0;
+  double ms = 0;
+  int rc = KVX_OK;
+  for (TimedLaunch& t : v) {
+    float e = 0;
+    cudaError_t err = cudaEventSynchronize(t.end);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&e, t.begin, t.end);
+    if (err != cudaSuccess && rc == KVX_OK) rc = cuda_error(err, "cudaEventElapsedTime");
+    cudaEventDestroy(t.begin);
+    cudaEventDestroy(t.end);
+    ++n;
+    ms += e;
+    bytes += t.hbm_bytes;
+  }
+  if (launches) *launches = n;
+  if (total_ms) *total_ms = ms;
+  if (hbm_bytes) *hbm_bytes = bytes;
+  return rc;
+}
 
 int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev, int64_t ce_min_run,
                   int64_t staging_bytes) {

@@ -201,6 +201,16 @@ int kvx_plan_swap(const int64_t* source_block_ids,
  * kvx_device_status: reads (and with reset != 0 clears) the device error word
  * written by kernels whose bounded waits gave up; synchronizes the device.  */
 int kvx_last_mode(void);
+/* Number of copy kernels this process has launched through the library. */
+uint64_t kvx_kernel_launches(void);
+/* Per-launch timing of the copy kernels: while enabled, every launch is
+ * bracketed by two CUDA events on its stream.  _read synchronizes those
+ * events and returns, since the previous read, the number of launches, their
+ * summed durations and the HBM bytes they move (read + write when both sides
+ * are local memory, one side when the other is host or peer memory). */
+int kvx_kernel_timing(int enable);
+int kvx_kernel_timing_read(uint64_t* launches, double* total_ms,
+                           uint64_t* hbm_bytes);
 int kvx_device_status(int device, int reset, int* status_out);
 
 /* Tuning knobs of KVX_MODE_AUTO and of the kernels; 0 keeps the current value.
