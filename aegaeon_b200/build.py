@@ -17,6 +17,7 @@ ROOT = os.path.dirname(HERE)
 SOURCES = [
     os.path.join(HERE, "csrc", "kvx_plan.cpp"),
     os.path.join(HERE, "csrc", "kvx_runtime.cu"),
+    os.path.join(HERE, "csrc", "kvx_noalloc.cu"),
 ]
 HEADERS = [
     os.path.join(HERE, "csrc", "kvx_plan.h"),

@@ -127,7 +127,7 @@ constexpr uint32_t kBulkChunk = 16384;  // one tile per stage
 constexpr uint32_t kBulkSmem = kBulkStages * kBulkChunk + kBulkStages * 8;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
 
-__device__ int g_kvx_device_status;
+static __device__ int g_kvx_device_status;
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -187,7 +187,7 @@ __device__ __forceinline__ void bulk_wait_all() {
 
 // Requires every item 16-byte aligned in address and length (the host checks)
 // and tile size == kBulkChunk.
-__global__ void __launch_bounds__(32)
+static __global__ void __launch_bounds__(32)
     kvx_copy_bulk(const Item* __restrict__ items, uint32_t n_items,
                   uint32_t n_tiles) {
   extern __shared__ __align__(128) unsigned char smem[];

@@ -558,6 +558,11 @@ int execute_host_copies(DeviceState* st, std::vector<Copy>& copies, bool is_swap
 }
 
 }  // namespace
+
+// Sets the message kvx_last_error() returns to this thread (used by the
+// entry points defined in other files of the library).
+void record_error(const std::string& msg) { t_last_error = msg; }
+
 }  // namespace kvx
 
 struct kvx_layout {

@@ -221,6 +221,31 @@ int kvx_device_status(int device, int reset, int* status_out);
 int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
                   int64_t ce_min_run, int64_t staging_bytes);
 
+/* ---- allocation-free swap ---------------------------------------------------
+ * No counterpart in the reference.  For callers that must not allocate GPU
+ * memory while they swap: a runtime that owns all of HBM through its own
+ * arena, a process swapping out near its memory limit during a model switch,
+ * or code where an allocation would synchronise the device.  Same copy as
+ * kvx_swap in its SM zero-copy mode (kv_swap must be page-locked and mapped
+ * for the device), same checks, same last-writer rule for repeated targets.
+ * Its scratch is a fixed device array of KVX_NOALLOC_MAX_IDS source and
+ * target ids (1 MiB), compiled into the library and held by every GPU that
+ * loads it until the process exits; more ids per call are rejected with
+ * KVX_ERR_INVALID_ARGUMENT (message in kvx_last_error).  Nothing is
+ * allocated: no cudaMalloc, cudaFree or allocating library call.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  All calls share the array and each call
+ * overwrites the ids it uses (nothing needs to start at zero): calls whose
+ * GPU work overlaps, e.g. on two streams without an event between them, race
+ * on it.  Calls on one stream are ordered and safe.                         */
+#define KVX_NOALLOC_MAX_IDS 65536
+int kvx_swap_noalloc(const int64_t* source_block_ids,
+                     const int64_t* target_block_ids, int64_t num_ids,
+                     int is_swap_in, void* kv_cache, uint64_t kv_cache_bytes,
+                     uint64_t block_bytes, void* kv_swap,
+                     uint64_t kv_swap_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
