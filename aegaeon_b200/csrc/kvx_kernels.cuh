@@ -22,6 +22,7 @@
 #include <cstdint>
 
 #include "kvx_plan.h"
+#include "kvx_worklist.h"
 
 namespace kvx {
 
@@ -101,29 +102,56 @@ __device__ __forceinline__ void cta_copy(const char* __restrict__ s,
   }
 }
 
-template <int kSrc>
+// A work list maps a tile index to (source, destination, length).  seek()
+// positions a cursor on the first tile of a CTA's span; get() advances the
+// cursor monotonically.
+struct ItemList {
+  const Item* items;
+  uint32_t n;
+  __device__ __forceinline__ uint32_t seek(uint32_t t) const { return find_item(items, n, t); }
+  __device__ __forceinline__ void get(uint32_t& cur, uint32_t t, uint32_t shift, uint64_t* src,
+                                      uint64_t* dst, uint32_t* len) const {
+    while (cur + 1 < n && items[cur + 1].tile_begin <= t) ++cur;
+    const Item it = items[cur];
+    const uint64_t off = uint64_t(t - it.tile_begin) << shift;
+    *len = uint32_t(min(uint64_t(it.len) - off, uint64_t(1) << shift));
+    *src = it.src + off;
+    *dst = it.dst + off;
+  }
+};
+
+struct GridList {
+  const GridEntry* entries;
+  uint32_t n;
+  const GridSeg* segs;
+  __device__ __forceinline__ uint32_t seek(uint32_t t) const { return grid_find(entries, n, t); }
+  __device__ __forceinline__ void get(uint32_t& cur, uint32_t t, uint32_t shift, uint64_t* src,
+                                      uint64_t* dst, uint32_t* len) const {
+    while (cur + 1 < n && entries[cur + 1].tile_begin <= t) ++cur;
+    grid_resolve(entries[cur], segs, t, shift, src, dst, len);
+  }
+};
+
+template <int kSrc, class List>
 __global__ void __launch_bounds__(kVecThreads)
-    kvx_copy_vec(const Item* __restrict__ items, uint32_t n_items,
-                 uint32_t n_tiles, uint32_t tile_shift) {
+    kvx_copy_vec(List list, uint32_t n_tiles, uint32_t tile_shift) {
   uint32_t t0, t1;
   cta_span(n_tiles, &t0, &t1);
   if (t0 >= t1) return;
-  uint32_t i = find_item(items, n_items, t0);
+  uint32_t cur = list.seek(t0);
   for (uint32_t t = t0; t < t1; ++t) {
-    while (i + 1 < n_items && items[i + 1].tile_begin <= t) ++i;
-    const Item it = items[i];
-    const uint64_t off = uint64_t(t - it.tile_begin) << tile_shift;
-    const uint64_t left = uint64_t(it.len) - off;
-    const uint32_t n = uint32_t(min(left, uint64_t(1) << tile_shift));
-    cta_copy<kSrc>(reinterpret_cast<const char*>(it.src + off),
-                   reinterpret_cast<char*>(it.dst + off), n);
+    uint64_t src, dst;
+    uint32_t n;
+    list.get(cur, t, tile_shift, &src, &dst, &n);
+    cta_copy<kSrc>(reinterpret_cast<const char*>(src), reinterpret_cast<char*>(dst), n);
   }
 }
 
 // ---- TMA bulk copy (local HBM only) ----------------------------------------
 
 constexpr int kBulkStages = 6;
-constexpr uint32_t kBulkChunk = 16384;  // one tile per stage
+constexpr uint32_t kBulkShift = 14;
+constexpr uint32_t kBulkChunk = 1u << kBulkShift;  // one tile per stage
 constexpr uint32_t kBulkSmem = kBulkStages * kBulkChunk + kBulkStages * 8;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
 
@@ -185,11 +213,10 @@ __device__ __forceinline__ void bulk_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
-// Requires every item 16-byte aligned in address and length (the host checks)
-// and tile size == kBulkChunk.
-static __global__ void __launch_bounds__(32)
-    kvx_copy_bulk(const Item* __restrict__ items, uint32_t n_items,
-                  uint32_t n_tiles) {
+// Requires every copy 16-byte aligned in address and length (the host checks)
+// and a tile size of kBulkChunk.
+template <class List>
+__global__ void __launch_bounds__(32) kvx_copy_bulk(List list, uint32_t n_tiles) {
   extern __shared__ __align__(128) unsigned char smem[];
   if (threadIdx.x != 0) return;
   uint32_t t0, t1;
@@ -206,20 +233,17 @@ static __global__ void __launch_bounds__(32)
 
   uint64_t st_dst[kBulkStages];
   uint32_t st_len[kBulkStages];
-  uint32_t li = find_item(items, n_items, t0);  // load-side item cursor
-  uint32_t next_load = 0;                        // chunks issued so far
+  uint32_t cur = list.seek(t0);  // load-side cursor
+  uint32_t next_load = 0;        // chunks issued so far
   auto issue_load = [&]() {
     const uint32_t k = next_load++;
-    const uint32_t t = t0 + k;
-    while (li + 1 < n_items && items[li + 1].tile_begin <= t) ++li;
-    const Item it = items[li];
-    const uint64_t off = uint64_t(t - it.tile_begin) * kBulkChunk;
-    const uint32_t n = uint32_t(min(uint64_t(it.len) - off, uint64_t(kBulkChunk)));
+    uint64_t src, dst;
+    uint32_t n;
+    list.get(cur, t0 + k, kBulkShift, &src, &dst, &n);
     const int s = int(k % kBulkStages);
-    st_dst[s] = it.dst + off;
+    st_dst[s] = dst;
     st_len[s] = n;
-    bulk_load(buf0 + s * kBulkChunk, reinterpret_cast<const void*>(it.src + off), n,
-              bar0 + 8 * s);
+    bulk_load(buf0 + s * kBulkChunk, reinterpret_cast<const void*>(src), n, bar0 + 8 * s);
   };
 
   while (next_load < T && next_load < uint32_t(kBulkStages)) issue_load();

@@ -140,6 +140,7 @@ Error plan_swap_blocks(const Layout& L, const Entries& e, bool is_swap_in,
   Error err = check_groups(L, e);
   if (!err.ok()) return err;
   const size_t ns = L.seg_pages.size();
+  out->reserve(ns * size_t(e.n));
   for (size_t s = 0; s < ns; ++s) {
     const uint64_t page = L.seg_page_bytes[s];
     const uint64_t owners = L.seg_owner_mask[s];
@@ -436,6 +437,225 @@ uint64_t mean_host_run(const std::vector<Copy>& copies, bool host_is_src) {
   for (size_t i = 1; i < hv.size(); ++i)
     if (hv[i - 1].first + hv[i - 1].second != hv[i].first) ++runs;
   return total / runs;
+}
+
+namespace {
+
+struct Range {
+  uint64_t b, e;
+};
+
+// True when no range of `a` intersects a range of `b`.
+bool disjoint_sets(std::vector<Range> a, std::vector<Range> b) {
+  auto by_begin = [](const Range& x, const Range& y) { return x.b < y.b; };
+  std::sort(a.begin(), a.end(), by_begin);
+  std::sort(b.begin(), b.end(), by_begin);
+  size_t i = 0, j = 0;
+  while (i < a.size() && j < b.size()) {
+    if (a[i].b >= a[i].e) { ++i; continue; }
+    if (b[j].b >= b[j].e) { ++j; continue; }
+    if (a[i].b < b[j].e && b[j].b < a[i].e) return false;
+    if (a[i].e <= b[j].e) ++i; else ++j;
+  }
+  return true;
+}
+
+bool unique_ids(std::vector<int64_t> ids) {
+  std::sort(ids.begin(), ids.end());
+  return std::adjacent_find(ids.begin(), ids.end()) == ids.end();
+}
+
+// Entry-level checks shared by the segmented grid builders: uniform page,
+// owners, groups, extents.  Fills out->entries (ids raw, extents set) and
+// returns false when the grid form does not apply.
+bool grid_entries(const Layout& L, const Entries& e, GridPlan* out, uint64_t* page_out) {
+  const size_t ns = L.seg_pages.size();
+  if (ns == 0 || e.n < 0 || (e.n > 0 && (!e.src || !e.dst || !e.group || !e.first || !e.valid)))
+    return false;
+  const uint64_t page = L.seg_page_bytes[0];
+  if (page == 0 || page >= (1ull << 32)) return false;
+  uint64_t common_owners = ~0ull;
+  for (size_t s = 0; s < ns; ++s) {
+    if (L.seg_page_bytes[s] != page) return false;
+    common_owners &= L.seg_owner_mask[s];
+  }
+  const int64_t ng = int64_t(L.group_ratio.size());
+  out->entries.clear();
+  out->entries.reserve(size_t(e.n));
+  for (int64_t i = 0; i < e.n; ++i) {
+    const int64_t g = e.group[i];
+    if (g < 0 || g >= ng) return false;
+    if (!((common_owners >> g) & 1)) return false;  // some segment skips this group
+    uint64_t off = 0, len = 0;
+    if (!byte_extent(page, L.group_ratio[g], e.first[i], e.valid[i], &off, &len).ok()) return false;
+    if (len == 0) continue;
+    GridEntry ge{e.src[i], e.dst[i], uint32_t(off), uint32_t(len), 0, 0};
+    out->entries.push_back(ge);
+  }
+  *page_out = page;
+  return true;
+}
+
+bool ids_in(const std::vector<GridEntry>& v, bool src, uint64_t limit) {
+  for (const GridEntry& g : v) {
+    const int64_t id = src ? g.src_id : g.dst_id;
+    if (id < 0 || uint64_t(id) >= limit) return false;
+  }
+  return true;
+}
+
+uint64_t min_blocks(const Layout& L) {
+  uint64_t m = ~0ull;
+  for (uint64_t b : L.seg_num_blocks) m = std::min(m, b);
+  return m;
+}
+
+std::vector<Range> page_ranges(const Layout& L) {
+  std::vector<Range> r;
+  for (size_t s = 0; s < L.seg_pages.size(); ++s)
+    r.push_back(Range{L.seg_pages[s], L.seg_pages[s] + L.seg_page_bytes[s] * L.seg_num_blocks[s]});
+  return r;
+}
+
+std::vector<int64_t> dst_ids(const std::vector<GridEntry>& v) {
+  std::vector<int64_t> d;
+  d.reserve(v.size());
+  for (const GridEntry& g : v) d.push_back(g.dst_id);
+  return d;
+}
+
+}  // namespace
+
+bool grid_swap_blocks(const Layout& L, const Entries& e, bool is_swap_in, uint64_t host_base,
+                      GridPlan* out) {
+  if (!L.host_pool || !host_base) return false;
+  uint64_t page = 0;
+  if (!grid_entries(L, e, out, &page)) return false;
+  const uint64_t dev_limit = min_blocks(L);
+  if (!ids_in(out->entries, !is_swap_in, dev_limit)) return false;
+  if (!ids_in(out->entries, is_swap_in, L.host_num_rows)) return false;
+  if (!unique_ids(dst_ids(out->entries))) return false;
+  const std::vector<Range> dev = page_ranges(L);
+  const std::vector<Range> host{Range{host_base, host_base + L.host_pool_bytes}};
+  if (!disjoint_sets(dev, host)) return false;
+  const size_t ns = L.seg_pages.size();
+  out->segs.clear();
+  const uint64_t row_base = host_base + L.host_row_offset;
+  for (size_t s = 0; s < ns; ++s) {
+    const uint64_t hb = row_base + L.seg_cpu_offset[s];
+    if (is_swap_in)
+      out->segs.push_back(GridSeg{hb, L.host_row_bytes, L.seg_pages[s], page});
+    else
+      out->segs.push_back(GridSeg{L.seg_pages[s], page, hb, L.host_row_bytes});
+  }
+  out->host_side = is_swap_in ? 1 : 2;
+  out->row_base = row_base;
+  out->row_stride = L.host_row_bytes;
+  // Whole, gap-free spans: full pages and cpu offsets tiling [0, S*page).
+  bool full = true;
+  for (const GridEntry& g : out->entries)
+    if (g.off != 0 || g.len != page) { full = false; break; }
+  if (full) {
+    std::vector<uint64_t> offs(L.seg_cpu_offset);
+    std::sort(offs.begin(), offs.end());
+    for (size_t s = 0; s < ns && full; ++s) full = offs[s] == s * page;
+  }
+  out->row_span = full ? ns * page : 0;
+  out->extents = out->entries.size() * ns;
+  out->copied = 0;
+  for (const GridEntry& g : out->entries) out->copied += uint64_t(g.len) * ns;
+  return true;
+}
+
+bool grid_migrate(const Layout& S, const Layout& T, const Entries& e, GridPlan* out) {
+  const size_t ns = S.seg_pages.size();
+  if (T.seg_pages.size() != ns || S.group_ratio != T.group_ratio) return false;
+  for (size_t s = 0; s < ns; ++s)
+    if (S.seg_page_bytes[s] != T.seg_page_bytes[s] || S.seg_owner_mask[s] != T.seg_owner_mask[s])
+      return false;
+  uint64_t page = 0;
+  if (!grid_entries(S, e, out, &page)) return false;
+  if (!ids_in(out->entries, true, min_blocks(S))) return false;
+  if (!ids_in(out->entries, false, min_blocks(T))) return false;
+  if (!unique_ids(dst_ids(out->entries))) return false;
+  if (!disjoint_sets(page_ranges(S), page_ranges(T))) return false;
+  out->segs.clear();
+  for (size_t s = 0; s < ns; ++s)
+    out->segs.push_back(GridSeg{S.seg_pages[s], page, T.seg_pages[s], page});
+  out->host_side = 0;
+  out->row_base = out->row_stride = out->row_span = 0;
+  out->extents = out->entries.size() * ns;
+  out->copied = 0;
+  for (const GridEntry& g : out->entries) out->copied += uint64_t(g.len) * ns;
+  return true;
+}
+
+bool grid_swap(const int64_t* src_ids, const int64_t* dst_ids_, int64_t n, bool is_swap_in,
+               uint64_t cache, uint64_t cache_bytes, uint64_t block_bytes, uint64_t swap,
+               uint64_t swap_bytes, GridPlan* out) {
+  if (n < 0 || (n > 0 && (!src_ids || !dst_ids_)) || block_bytes == 0 ||
+      block_bytes >= (1ull << 32) || !cache || !swap)
+    return false;
+  const uint64_t cache_blocks = cache_bytes / block_bytes;
+  const uint64_t swap_blocks = swap_bytes / block_bytes;
+  out->entries.clear();
+  out->entries.reserve(size_t(n));
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t dev = is_swap_in ? dst_ids_[i] : src_ids[i];
+    const int64_t slot = is_swap_in ? src_ids[i] : dst_ids_[i];
+    if (dev < 0 || uint64_t(dev) >= cache_blocks) return false;
+    if (slot < 0 || uint64_t(slot) >= swap_blocks) return false;
+    out->entries.push_back(GridEntry{src_ids[i], dst_ids_[i], 0, uint32_t(block_bytes), 0, 0});
+  }
+  if (!unique_ids(dst_ids(out->entries))) return false;
+  if (!disjoint_sets({Range{cache, cache + cache_blocks * block_bytes}},
+                     {Range{swap, swap + swap_blocks * block_bytes}}))
+    return false;
+  out->segs.clear();
+  if (is_swap_in)
+    out->segs.push_back(GridSeg{swap, block_bytes, cache, block_bytes});
+  else
+    out->segs.push_back(GridSeg{cache, block_bytes, swap, block_bytes});
+  out->host_side = is_swap_in ? 1 : 2;
+  out->row_base = swap;
+  out->row_stride = block_bytes;
+  out->row_span = block_bytes;
+  out->extents = out->entries.size();
+  out->copied = out->entries.size() * block_bytes;
+  return true;
+}
+
+uint64_t grid_finalize(GridPlan* p, uint32_t tile_shift) {
+  const uint64_t ns = p->segs.size();
+  uint64_t tiles = 0;
+  for (GridEntry& g : p->entries) {
+    const uint64_t per = (uint64_t(g.len) + (1ull << tile_shift) - 1) >> tile_shift;
+    g.tile_begin = uint32_t(tiles);
+    g.tiles_per_seg = uint32_t(per);
+    tiles += per * ns;
+    if (tiles > 0xffffffffull) return tiles;
+  }
+  return tiles;
+}
+
+void grid_expand(const GridPlan& p, uint32_t tile_shift, std::vector<Copy>* out) {
+  out->clear();
+  const uint32_t n = uint32_t(p.entries.size());
+  if (n == 0) return;
+  const GridEntry& last = p.entries.back();
+  const uint64_t tiles = uint64_t(last.tile_begin) + uint64_t(last.tiles_per_seg) * p.segs.size();
+  uint32_t cur = grid_find(p.entries.data(), n, 0);
+  for (uint64_t t = 0; t < tiles; ++t) {
+    while (cur + 1 < n && p.entries[cur + 1].tile_begin <= t) ++cur;
+    uint64_t src, dst;
+    uint32_t len;
+    grid_resolve(p.entries[cur], p.segs.data(), uint32_t(t), tile_shift, &src, &dst, &len);
+    if (!out->empty() && out->back().src + out->back().len == src &&
+        out->back().dst + out->back().len == dst)
+      out->back().len += len;
+    else
+      out->push_back(Copy{src, dst, len});
+  }
 }
 
 }  // namespace kvx

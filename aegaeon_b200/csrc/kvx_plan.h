@@ -7,6 +7,8 @@
 #include <string>
 #include <vector>
 
+#include "kvx_worklist.h"
+
 namespace kvx {
 
 // One byte-range copy. Addresses are absolute (device-visible for the kernel
@@ -115,5 +117,40 @@ void plan_staged(const std::vector<Copy>& copies, bool host_is_src,
 
 // Mean length of host-contiguous runs (after sorting by host address).
 uint64_t mean_host_run(const std::vector<Copy>& copies, bool host_is_src);
+
+// ---- grid plans (entries x segments expanded on the device) ----------------
+// A grid plan exists when every segment has the same page size, every
+// segment is owned by every cache group the entries use, the target ids of
+// the copying entries are distinct and the source and destination memory do
+// not overlap.  Then no two copies conflict and host work is O(entries).
+// The grid_* builders return false when those conditions do not hold or any
+// check fails: the item planner then runs and reports the canonical error.
+struct GridPlan {
+  std::vector<GridEntry> entries;
+  std::vector<GridSeg> segs;
+  uint64_t copied = 0;   // payload bytes
+  uint64_t extents = 0;  // entry x segment copies
+  // Host side, for swaps (0 for migrations): 1 = source, 2 = destination.
+  int host_side = 0;
+  uint64_t row_base = 0;    // host address of row 0 of this GPU's bytes
+  uint64_t row_stride = 0;  // host row pitch
+  uint64_t row_span = 0;    // S * page when every entry writes its whole,
+                            // gap-free composite span (copy-engine staging), else 0
+};
+
+bool grid_swap_blocks(const Layout& L, const Entries& e, bool is_swap_in,
+                      uint64_t host_base, GridPlan* out);
+bool grid_migrate(const Layout& S, const Layout& T, const Entries& e, GridPlan* out);
+bool grid_swap(const int64_t* src_ids, const int64_t* dst_ids, int64_t n, bool is_swap_in,
+               uint64_t cache, uint64_t cache_bytes, uint64_t block_bytes, uint64_t swap,
+               uint64_t swap_bytes, GridPlan* out);
+
+// Fill tile_begin / tiles_per_seg for a tile size of 1 << tile_shift and
+// return the tile count (> 0xffffffff: too large for one launch).
+uint64_t grid_finalize(GridPlan* p, uint32_t tile_shift);
+
+// The copies a finalized grid plan performs, tile by tile, through the same
+// resolver the kernels use (host emulation; tiles of one copy are merged).
+void grid_expand(const GridPlan& p, uint32_t tile_shift, std::vector<Copy>* out);
 
 }  // namespace kvx

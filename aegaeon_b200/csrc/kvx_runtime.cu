@@ -282,14 +282,26 @@ bool all_aligned16(const std::vector<Copy>& v) {
   return true;
 }
 
-// Item table of several launches, uploaded once.
+// Tables of every launch of one call, uploaded with one copy.
+struct Upload {
+  std::vector<char> bytes;
+  size_t add(const void* p, size_t n) {
+    const size_t off = (bytes.size() + 255) & ~size_t(255);
+    bytes.resize(off + n);
+    if (n) std::memcpy(bytes.data() + off, p, n);
+    return off;
+  }
+};
+
 struct Launch {
-  size_t item_off;   // index into the combined item vector
-  uint32_t n_items;
-  uint32_t n_tiles;
-  bool bulk;
-  Path path;
-  uint64_t bytes;    // payload bytes of this launch
+  bool grid = false;     // grid list (entries x segments) or item list
+  size_t table_off = 0;  // byte offset of the items / grid entries in the upload
+  size_t segs_off = 0;   // grid: byte offset of the segment table
+  uint32_t n = 0;        // items or entries
+  uint32_t n_tiles = 0;
+  bool bulk = false;
+  Path path = Path::kDevice;
+  uint64_t bytes = 0;    // payload bytes of this launch
 };
 
 // HBM bytes a launch moves on this GPU: read + write when both sides are
@@ -304,101 +316,172 @@ uint64_t payload_of(const std::vector<Copy>& v) {
   return b;
 }
 
-int upload_items(DeviceState* st, const std::vector<Item>& items,
-                 cudaStream_t s, size_t* ring_off) {
-  const size_t bytes = items.size() * sizeof(Item);
+int upload(DeviceState* st, const Upload& up, cudaStream_t s, size_t* ring_off) {
+  const size_t bytes = up.bytes.size();
   int rc = ring_acquire(st, bytes ? bytes : 256, ring_off);
   if (rc) return rc;
   if (bytes) {
-    std::memcpy(st->ring_host + *ring_off, items.data(), bytes);
-    KVX_CUDA(cudaMemcpyAsync(st->ring_dev + *ring_off, st->ring_host + *ring_off,
-                             bytes, cudaMemcpyHostToDevice, s));
+    std::memcpy(st->ring_host + *ring_off, up.bytes.data(), bytes);
+    KVX_CUDA(cudaMemcpyAsync(st->ring_dev + *ring_off, st->ring_host + *ring_off, bytes,
+                             cudaMemcpyHostToDevice, s));
   }
   return KVX_OK;
 }
 
+int release(DeviceState* st, size_t ring_off, const Upload& up, cudaStream_t s) {
+  return ring_release_on(st, ring_off, up.bytes.size() ? up.bytes.size() : 256, s);
+}
+
 int ensure_bulk(DeviceState* st) {
   if (st->bulk_ready) return KVX_OK;
-  KVX_CUDA(cudaFuncSetAttribute(kvx_copy_bulk,
-                                cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(kBulkSmem)));
+  KVX_CUDA(cudaFuncSetAttribute(kvx_copy_bulk<ItemList>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, int(kBulkSmem)));
+  KVX_CUDA(cudaFuncSetAttribute(kvx_copy_bulk<GridList>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, int(kBulkSmem)));
   st->bulk_ready = true;
   return KVX_OK;
 }
 
-int launch_kernel(DeviceState* st, const Item* dev_items, const Launch& l,
-                  cudaStream_t s, const Tunables& tn);
+constexpr uint32_t kVecShift = 15;
+constexpr uint32_t kVecTile = 1u << kVecShift;  // 32 KiB
 
-int launch_one(DeviceState* st, const Item* dev_items, const Launch& l,
-               cudaStream_t s, const Tunables& tn) {
+template <class List>
+void launch_list(const List& list, const Launch& l, const DeviceState* st, cudaStream_t s,
+                 const Tunables& tn) {
+  if (l.bulk) {
+    // Two 96 KiB CTAs fit on an SM.
+    const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(2 * st->sms));
+    kvx_copy_bulk<List><<<grid, 32, kBulkSmem, s>>>(list, l.n_tiles);
+  } else {
+    const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(ctas_for(st, l.path, tn)));
+    if (l.path == Path::kHostSrc)
+      kvx_copy_vec<kSrcHost, List><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles, kVecShift);
+    else
+      kvx_copy_vec<kSrcDevice, List><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles, kVecShift);
+  }
+}
+
+int launch_kernel(DeviceState* st, size_t ring_off, const Launch& l, cudaStream_t s,
+                  const Tunables& tn) {
+  if (l.bulk) {
+    int rc = ensure_bulk(st);
+    if (rc) return rc;
+  }
+  const char* base = st->ring_dev + ring_off;
+  if (l.grid)
+    launch_list(GridList{reinterpret_cast<const GridEntry*>(base + l.table_off), l.n,
+                         reinterpret_cast<const GridSeg*>(base + l.segs_off)},
+                l, st, s, tn);
+  else
+    launch_list(ItemList{reinterpret_cast<const Item*>(base + l.table_off), l.n}, l, st, s, tn);
+  KVX_CUDA(cudaGetLastError());
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+  return KVX_OK;
+}
+
+int launch_one(DeviceState* st, size_t ring_off, const Launch& l, cudaStream_t s,
+               const Tunables& tn) {
   if (l.n_tiles == 0) return KVX_OK;
-  if (!g_timing.load(std::memory_order_relaxed)) return launch_kernel(st, dev_items, l, s, tn);
+  if (!g_timing.load(std::memory_order_relaxed)) return launch_kernel(st, ring_off, l, s, tn);
   TimedLaunch t{st->device, nullptr, nullptr, hbm_bytes_of(l)};
   KVX_CUDA(cudaEventCreate(&t.begin));
   KVX_CUDA(cudaEventCreate(&t.end));
   KVX_CUDA(cudaEventRecord(t.begin, s));
-  int rc = launch_kernel(st, dev_items, l, s, tn);
+  int rc = launch_kernel(st, ring_off, l, s, tn);
   KVX_CUDA(cudaEventRecord(t.end, s));
   std::lock_guard<std::mutex> g(g_timing_mu);
   g_timed.push_back(t);
   return rc;
 }
 
-int launch_kernel(DeviceState* st, const Item* dev_items, const Launch& l,
-                  cudaStream_t s, const Tunables& tn) {
-  if (l.bulk) {
-    int rc = ensure_bulk(st);
-    if (rc) return rc;
-    // Two 96 KiB CTAs fit on an SM.
-    const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(2 * st->sms));
-    kvx_copy_bulk<<<grid, 32, kBulkSmem, s>>>(dev_items, l.n_items, l.n_tiles);
-  } else {
-    const uint32_t grid =
-        std::min<uint32_t>(l.n_tiles, uint32_t(ctas_for(st, l.path, tn)));
-    if (l.path == Path::kHostSrc)
-      kvx_copy_vec<kSrcHost><<<grid, kVecThreads, 0, s>>>(dev_items, l.n_items,
-                                                          l.n_tiles, 15);
-    else
-      kvx_copy_vec<kSrcDevice><<<grid, kVecThreads, 0, s>>>(dev_items, l.n_items,
-                                                            l.n_tiles, 15);
-  }
-  KVX_CUDA(cudaGetLastError());
-  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+// Append an item-list launch for `copies` (one wave, coalesced by the caller).
+int add_items(Upload* up, std::vector<Launch>* launches, const std::vector<Copy>& copies,
+              Path path, bool bulk) {
+  std::vector<Item> items;
+  const uint64_t tiles = build_items(copies, bulk ? kBulkChunk : kVecTile, &items);
+  if (tiles > 0xffffffffull)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "request too large for one launch");
+  Launch l;
+  l.table_off = up->add(items.data(), items.size() * sizeof(Item));
+  l.n = uint32_t(items.size());
+  l.n_tiles = uint32_t(tiles);
+  l.bulk = bulk;
+  l.path = path;
+  l.bytes = payload_of(copies);
+  launches->push_back(l);
   return KVX_OK;
 }
 
-constexpr uint32_t kVecTile = 1u << 15;  // 32 KiB
+bool grid_aligned16(const GridPlan& p) {
+  for (const GridSeg& g : p.segs)
+    if ((g.src_base | g.src_stride | g.dst_base | g.dst_stride) & 15) return false;
+  for (const GridEntry& e : p.entries)
+    if ((e.off | e.len) & 15) return false;
+  return true;
+}
+
+// Append a grid launch (finalizes `p` for the chosen tile size).
+int add_grid(Upload* up, std::vector<Launch>* launches, GridPlan* p, Path path, bool bulk) {
+  const uint64_t tiles = grid_finalize(p, bulk ? kBulkShift : kVecShift);
+  if (tiles > 0xffffffffull)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "request too large for one launch");
+  Launch l;
+  l.grid = true;
+  l.table_off = up->add(p->entries.data(), p->entries.size() * sizeof(GridEntry));
+  l.segs_off = up->add(p->segs.data(), p->segs.size() * sizeof(GridSeg));
+  l.n = uint32_t(p->entries.size());
+  l.n_tiles = uint32_t(tiles);
+  l.bulk = bulk;
+  l.path = path;
+  l.bytes = p->copied;
+  launches->push_back(l);
+  return KVX_OK;
+}
+
+int run_launches(DeviceState* st, const Upload& up, const std::vector<Launch>& launches,
+                 cudaStream_t s, const Tunables& tn) {
+  size_t off = 0;
+  int rc = upload(st, up, s, &off);
+  if (rc) return rc;
+  for (const Launch& l : launches) {
+    rc = launch_one(st, off, l, s, tn);
+    if (rc) return rc;
+  }
+  return release(st, off, up, s);
+}
 
 // Run waves of device-visible copies through the SM kernels (one launch per
 // wave, one descriptor upload for all of them).
 int run_sm(DeviceState* st, const std::vector<Copy>& copies,
            const std::vector<size_t>& waves, Path path, bool allow_bulk,
            cudaStream_t s, const Tunables& tn) {
-  std::vector<Item> all;
+  Upload up;
   std::vector<Launch> launches;
-  std::vector<Item> tmp;
   size_t begin = 0;
   for (size_t end : waves) {
     std::vector<Copy> w(copies.begin() + begin, copies.begin() + end);
     begin = end;
     coalesce(&w);
     const bool bulk = allow_bulk && path == Path::kDevice && all_aligned16(w);
-    const uint64_t tiles = build_items(w, bulk ? kBulkChunk : kVecTile, &tmp);
-    if (tiles > 0xffffffffull)
-      return set_error(KVX_ERR_INVALID_ARGUMENT, "request too large for one launch");
-    launches.push_back(Launch{all.size(), uint32_t(tmp.size()), uint32_t(tiles), bulk, path,
-                              payload_of(w)});
-    all.insert(all.end(), tmp.begin(), tmp.end());
-  }
-  size_t off = 0;
-  int rc = upload_items(st, all, s, &off);
-  if (rc) return rc;
-  const Item* base = reinterpret_cast<const Item*>(st->ring_dev + off);
-  for (const Launch& l : launches) {
-    rc = launch_one(st, base + l.item_off, l, s, tn);
+    int rc = add_items(&up, &launches, w, path, bulk);
     if (rc) return rc;
   }
-  return ring_release_on(st, off, all.size() * sizeof(Item), s);
+  return run_launches(st, up, launches, s, tn);
+}
+
+// One grid launch through the SM kernels.
+int run_sm_grid(DeviceState* st, GridPlan* p, Path path, bool allow_bulk, cudaStream_t s,
+                const Tunables& tn) {
+  Upload up;
+  std::vector<Launch> launches;
+  const bool bulk = allow_bulk && path == Path::kDevice && grid_aligned16(*p);
+  int rc = add_grid(&up, &launches, p, path, bulk);
+  if (rc) return rc;
+  return run_launches(st, up, launches, s, tn);
+}
+
+size_t staging_cap(const Tunables& tn) {
+  return size_t(std::max<int64_t>(tn.staging_bytes, 1 << 20)) & ~size_t(4095);
 }
 
 // Copy-engine path through a staging area.  `copies` use the caller's host
@@ -406,17 +489,14 @@ int run_sm(DeviceState* st, const std::vector<Copy>& copies,
 int run_ce_staged(DeviceState* st, const std::vector<Copy>& copies,
                   const std::vector<size_t>& waves, bool host_is_src,
                   bool allow_bulk, cudaStream_t s, const Tunables& tn) {
-  const size_t cap = size_t(std::max<int64_t>(tn.staging_bytes, 1 << 20)) & ~size_t(4095);
-  uint64_t total = 0;
-  for (const Copy& c : copies) total += c.len;
-  if (total == 0) return KVX_OK;
+  if (payload_of(copies) == 0) return KVX_OK;
   Staging* sg = nullptr;
-  int rc = staging_get(st, host_is_src ? 1 : 0, cap, s, &sg);
+  int rc = staging_get(st, host_is_src ? 1 : 0, staging_cap(tn), s, &sg);
   if (rc) return rc;
   const uint64_t sbase = reinterpret_cast<uint64_t>(sg->dev);
   // Build every chunk's item table first (one upload).
-  std::vector<std::vector<StagedChunk>> plans;
-  std::vector<Item> all, tmp;
+  std::vector<StagedChunk> all_chunks;
+  Upload up;
   std::vector<Launch> launches;
   size_t begin = 0;
   for (size_t end : waves) {
@@ -426,40 +506,131 @@ int run_ce_staged(DeviceState* st, const std::vector<Copy>& copies,
     plan_staged(w, host_is_src, sg->cap, &chunks);
     for (StagedChunk& ch : chunks) {
       for (Copy& m : ch.device_moves) (host_is_src ? m.src : m.dst) += sbase;
-      const bool bulk = allow_bulk && all_aligned16(ch.device_moves);
-      const uint64_t tiles = build_items(ch.device_moves, bulk ? kBulkChunk : kVecTile, &tmp);
-      launches.push_back(Launch{all.size(), uint32_t(tmp.size()), uint32_t(tiles), bulk,
-                                Path::kDevice, payload_of(ch.device_moves)});
-      all.insert(all.end(), tmp.begin(), tmp.end());
+      rc = add_items(&up, &launches, ch.device_moves, Path::kDevice,
+                     allow_bulk && all_aligned16(ch.device_moves));
+      if (rc) return rc;
+      all_chunks.push_back(std::move(ch));
     }
-    plans.push_back(std::move(chunks));
   }
   size_t off = 0;
-  rc = upload_items(st, all, s, &off);
+  rc = upload(st, up, s, &off);
   if (rc) return rc;
-  const Item* base = reinterpret_cast<const Item*>(st->ring_dev + off);
-  size_t li = 0;
-  for (const auto& chunks : plans) {
-    for (const StagedChunk& ch : chunks) {
-      const Launch& l = launches[li++];
-      if (host_is_src) {
-        for (const Copy& r : ch.host_runs)
-          KVX_CUDA(cudaMemcpyAsync(sg->dev + r.dst, reinterpret_cast<const void*>(r.src),
-                                   r.len, cudaMemcpyHostToDevice, s));
-        rc = launch_one(st, base + l.item_off, l, s, tn);
-        if (rc) return rc;
-      } else {
-        rc = launch_one(st, base + l.item_off, l, s, tn);
-        if (rc) return rc;
-        for (const Copy& r : ch.host_runs)
-          KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.dst), sg->dev + r.src,
-                                   r.len, cudaMemcpyDeviceToHost, s));
-      }
+  for (size_t i = 0; i < all_chunks.size(); ++i) {
+    const StagedChunk& ch = all_chunks[i];
+    if (host_is_src) {
+      for (const Copy& r : ch.host_runs)
+        KVX_CUDA(cudaMemcpyAsync(sg->dev + r.dst, reinterpret_cast<const void*>(r.src), r.len,
+                                 cudaMemcpyHostToDevice, s));
+      rc = launch_one(st, off, launches[i], s, tn);
+      if (rc) return rc;
+    } else {
+      rc = launch_one(st, off, launches[i], s, tn);
+      if (rc) return rc;
+      for (const Copy& r : ch.host_runs)
+        KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.dst), sg->dev + r.src, r.len,
+                                 cudaMemcpyDeviceToHost, s));
     }
   }
   KVX_CUDA(cudaEventRecord(sg->last, s));
   sg->used = true;
-  return ring_release_on(st, off, all.size() * sizeof(Item), s);
+  return release(st, off, up, s);
+}
+
+// Host ids of a swap grid plan, sorted, with the order of the entries.
+std::vector<std::pair<int64_t, uint32_t>> host_order(const GridPlan& p) {
+  std::vector<std::pair<int64_t, uint32_t>> v;
+  v.reserve(p.entries.size());
+  for (uint32_t i = 0; i < p.entries.size(); ++i)
+    v.emplace_back(p.host_side == 1 ? p.entries[i].src_id : p.entries[i].dst_id, i);
+  std::sort(v.begin(), v.end());
+  return v;
+}
+
+// Mean bytes of the host-contiguous runs of a swap grid plan.
+uint64_t grid_mean_run(const GridPlan& p) {
+  if (p.entries.empty() || !p.row_span) return 0;
+  const auto v = host_order(p);
+  uint64_t runs = 1;
+  for (size_t i = 1; i < v.size(); ++i)
+    if (!(p.row_stride == p.row_span && v[i].first == v[i - 1].first + 1)) ++runs;
+  return p.copied / runs;
+}
+
+// Copy-engine path for a swap grid plan whose entries write whole composite
+// spans: the device side gathers (swap-out) or scatters (swap-in) a grid into
+// a staging area laid out as consecutive spans in host-row order; one
+// cudaMemcpyAsync per run of consecutive host rows moves it over the link.
+int run_ce_grid(DeviceState* st, const GridPlan& p, cudaStream_t s, const Tunables& tn) {
+  const bool host_is_src = p.host_side == 1;
+  const uint64_t span = p.row_span;
+  Staging* sg = nullptr;
+  int rc = staging_get(st, host_is_src ? 1 : 0, staging_cap(tn), s, &sg);
+  if (rc) return rc;
+  const uint64_t rows = sg->cap / span;
+  const uint64_t sbase = reinterpret_cast<uint64_t>(sg->dev);
+  const auto order = host_order(p);
+  // Staging segment table: segment s sits at its cpu offset inside a span.
+  std::vector<GridSeg> ssegs = p.segs;
+  for (GridSeg& g : ssegs) {
+    if (host_is_src) {
+      g.src_base = sbase + (g.src_base - p.row_base);
+      g.src_stride = span;
+    } else {
+      g.dst_base = sbase + (g.dst_base - p.row_base);
+      g.dst_stride = span;
+    }
+  }
+  struct Run {
+    uint64_t host, staging, len;
+  };
+  std::vector<std::vector<Run>> runs;
+  Upload up;
+  std::vector<Launch> launches;
+  for (size_t c0 = 0; c0 < order.size(); c0 += rows) {
+    const size_t c1 = std::min<size_t>(order.size(), c0 + rows);
+    GridPlan chunk;
+    chunk.segs = ssegs;
+    chunk.entries.reserve(c1 - c0);
+    std::vector<Run> rr;
+    for (size_t k = c0; k < c1; ++k) {
+      GridEntry e = p.entries[order[k].second];
+      const int64_t pos = int64_t(k - c0);
+      if (host_is_src) e.src_id = pos; else e.dst_id = pos;
+      chunk.entries.push_back(e);
+      chunk.copied += uint64_t(e.len) * ssegs.size();
+      const uint64_t h = p.row_base + uint64_t(order[k].first) * p.row_stride;
+      const uint64_t st_off = uint64_t(pos) * span;
+      if (!rr.empty() && rr.back().host + rr.back().len == h &&
+          rr.back().staging + rr.back().len == st_off)
+        rr.back().len += span;
+      else
+        rr.push_back(Run{h, st_off, span});
+    }
+    rc = add_grid(&up, &launches, &chunk, Path::kDevice, grid_aligned16(chunk));
+    if (rc) return rc;
+    runs.push_back(std::move(rr));
+  }
+  size_t off = 0;
+  rc = upload(st, up, s, &off);
+  if (rc) return rc;
+  for (size_t i = 0; i < launches.size(); ++i) {
+    if (host_is_src) {
+      for (const Run& r : runs[i])
+        KVX_CUDA(cudaMemcpyAsync(sg->dev + r.staging, reinterpret_cast<const void*>(r.host),
+                                 r.len, cudaMemcpyHostToDevice, s));
+      rc = launch_one(st, off, launches[i], s, tn);
+      if (rc) return rc;
+    } else {
+      rc = launch_one(st, off, launches[i], s, tn);
+      if (rc) return rc;
+      for (const Run& r : runs[i])
+        KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.host), sg->dev + r.staging, r.len,
+                                 cudaMemcpyDeviceToHost, s));
+    }
+  }
+  KVX_CUDA(cudaEventRecord(sg->last, s));
+  sg->used = true;
+  return release(st, off, up, s);
 }
 
 // One copy-engine copy per coalesced extent (no staging, no kernel).
@@ -476,6 +647,15 @@ int run_ce_extent(const std::vector<Copy>& copies, const std::vector<size_t>& wa
                                cudaMemcpyDefault, s));
   }
   return KVX_OK;
+}
+
+// The (entry x segment) copies of a grid plan, for the paths that need a copy
+// list (one copy per entry and segment).
+std::vector<Copy> grid_copies(GridPlan p) {
+  grid_finalize(&p, 31);
+  std::vector<Copy> v;
+  grid_expand(p, 31, &v);
+  return v;
 }
 
 // Host memory facts for the SM path.
@@ -550,6 +730,50 @@ int execute_host_copies(DeviceState* st, std::vector<Copy>& copies, bool is_swap
     rc = run_ce_staged(st, copies, waves, is_swap_in, true, s, tn);
   } else if (mode == KVX_MODE_CE_EXTENT) {
     rc = run_ce_extent(copies, waves, s);
+  } else {
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "unknown transfer mode " + std::to_string(mode));
+  }
+  if (rc == KVX_OK) t_last_mode = mode;
+  return rc;
+}
+
+// Execute a swap grid plan (built with the caller's host addresses).
+int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
+                      uint64_t host_caller_base, int mode, cudaStream_t s) {
+  const Tunables tn = tunables();
+  const bool is_swap_in = p->host_side == 1;
+  if (p->entries.empty()) {
+    t_last_mode = mode == KVX_MODE_AUTO ? KVX_MODE_SM : mode;
+    return KVX_OK;
+  }
+  if (mode == KVX_MODE_AUTO) {
+    if (!hi.mapped)
+      mode = KVX_MODE_CE;
+    else
+      mode = (tn.ce_min_run > 0 && p->row_span && grid_mean_run(*p) >= uint64_t(tn.ce_min_run))
+                 ? KVX_MODE_CE
+                 : KVX_MODE_SM;
+  }
+  if (mode == KVX_MODE_SM_BULK) mode = KVX_MODE_SM;  // bulk is device-only
+  int rc;
+  if (mode == KVX_MODE_SM) {
+    if (!hi.mapped)
+      return set_error(KVX_ERR_HOST_MEMORY,
+                       "host buffer is not page-locked/device-mapped; the SM mode "
+                       "needs cudaHostAlloc or cudaHostRegister memory");
+    const uint64_t delta = hi.dev_base - host_caller_base;  // modular
+    for (GridSeg& g : p->segs) (is_swap_in ? g.src_base : g.dst_base) += delta;
+    rc = run_sm_grid(st, p, is_swap_in ? Path::kHostSrc : Path::kHostDst, false, s, tn);
+  } else if (mode == KVX_MODE_CE) {
+    if (p->row_span && p->row_span <= staging_cap(tn)) {
+      rc = run_ce_grid(st, *p, s, tn);
+    } else {
+      const std::vector<Copy> v = grid_copies(*p);
+      rc = run_ce_staged(st, v, {v.size()}, is_swap_in, true, s, tn);
+    }
+  } else if (mode == KVX_MODE_CE_EXTENT) {
+    const std::vector<Copy> v = grid_copies(*p);
+    rc = run_ce_extent(v, {v.size()}, s);
   } else {
     return set_error(KVX_ERR_INVALID_ARGUMENT, "unknown transfer mode " + std::to_string(mode));
   }
@@ -657,10 +881,17 @@ int kvx_plan_swap(const int64_t* source_block_ids, const int64_t* target_block_i
   t_last_error.clear();
   if (!num_copies_inout) return set_error(KVX_ERR_INVALID_ARGUMENT, "null count");
   std::vector<Copy> copies;
-  int rc = from_plan(plan_swap(source_block_ids, target_block_ids, num_ids, is_swap_in != 0,
-                               kv_cache, kv_cache_bytes, block_bytes, kv_swap,
-                               kv_swap_bytes, &copies));
-  if (rc) return rc;
+  GridPlan gp;
+  if (grid_swap(source_block_ids, target_block_ids, num_ids, is_swap_in != 0, kv_cache,
+                kv_cache_bytes, block_bytes, kv_swap, kv_swap_bytes, &gp)) {
+    grid_finalize(&gp, kVecShift);
+    grid_expand(gp, kVecShift, &copies);
+  } else {
+    int rc = from_plan(plan_swap(source_block_ids, target_block_ids, num_ids, is_swap_in != 0,
+                                 kv_cache, kv_cache_bytes, block_bytes, kv_swap,
+                                 kv_swap_bytes, &copies));
+    if (rc) return rc;
+  }
   const int64_t cap = *num_copies_inout;
   *num_copies_inout = int64_t(copies.size());
   if (cap < int64_t(copies.size()) || !src_addrs || !dst_addrs || !lengths) return KVX_OK;
@@ -695,7 +926,14 @@ int kvx_swap(const int64_t* source_block_ids, const int64_t* target_block_ids,
   rc = get_state(device, &st);
   if (rc) return rc;
   const HostInfo hi = host_info(kv_swap, device);
+  GridPlan gp;
+  const bool grid = grid_swap(source_block_ids, target_block_ids, num_ids, is_swap_in != 0,
+                              reinterpret_cast<uint64_t>(kv_cache), kv_cache_bytes, block_bytes,
+                              reinterpret_cast<uint64_t>(kv_swap), kv_swap_bytes, &gp);
   std::lock_guard<std::mutex> g(st->mu);
+  if (grid)
+    return execute_grid_host(st, &gp, hi, reinterpret_cast<uint64_t>(kv_swap), mode,
+                             reinterpret_cast<cudaStream_t>(stream));
   return execute_host_copies(st, copies, is_swap_in != 0, hi,
                              reinterpret_cast<uint64_t>(kv_swap), mode,
                              reinterpret_cast<cudaStream_t>(stream));
@@ -763,9 +1001,15 @@ int kvx_plan_swap_blocks(const kvx_layout* layout, int64_t num_entries,
   Entries e{num_entries, source_block_ids, target_block_ids, group_ids,
             first_kernel_blocks, valid_kernel_blocks};
   std::vector<Copy> copies;
-  int rc = from_plan(plan_swap_blocks(layout->L, e, is_swap_in != 0, layout->L.host_pool,
-                                      &copies, nullptr));
-  if (rc) return rc;
+  GridPlan gp;
+  if (grid_swap_blocks(layout->L, e, is_swap_in != 0, layout->L.host_pool, &gp)) {
+    grid_finalize(&gp, kVecShift);
+    grid_expand(gp, kVecShift, &copies);
+  } else {
+    int rc = from_plan(plan_swap_blocks(layout->L, e, is_swap_in != 0, layout->L.host_pool,
+                                        &copies, nullptr));
+    if (rc) return rc;
+  }
   const int64_t cap = *num_copies_inout;
   *num_copies_inout = int64_t(copies.size());
   if (cap < int64_t(copies.size()) || !src_addrs || !dst_addrs || !lengths) return KVX_OK;
@@ -786,14 +1030,25 @@ int kvx_swap_blocks(kvx_layout* layout, int64_t num_entries,
   if (!layout) return set_error(KVX_ERR_INVALID_ARGUMENT, "null layout");
   Entries e{num_entries, source_block_ids, target_block_ids, group_ids,
             first_kernel_blocks, valid_kernel_blocks};
+  // Grid form first (O(entries) host work); the item planner otherwise, which
+  // is also the one that reports invalid requests.
+  GridPlan gp;
+  const bool grid = grid_swap_blocks(layout->L, e, is_swap_in != 0, layout->L.host_pool, &gp);
   std::vector<Copy> copies;
-  uint64_t copied = 0;
-  int rc = from_plan(plan_swap_blocks(layout->L, e, is_swap_in != 0, layout->L.host_pool,
-                                      &copies, &copied));
-  if (rc) return rc;
+  uint64_t copied = 0, extents = 0;
+  int rc = KVX_OK;
+  if (grid) {
+    copied = gp.copied;
+    extents = gp.extents;
+  } else {
+    rc = from_plan(plan_swap_blocks(layout->L, e, is_swap_in != 0, layout->L.host_pool,
+                                    &copies, &copied));
+    if (rc) return rc;
+    extents = copies.size();
+  }
   if (copied_bytes) *copied_bytes = copied;
-  if (copy_extents) *copy_extents = copies.size();
-  if (copies.empty()) {
+  if (copy_extents) *copy_extents = extents;
+  if (extents == 0) {
     t_last_mode = mode == KVX_MODE_AUTO ? KVX_MODE_SM : mode;
     return KVX_OK;
   }
@@ -807,6 +1062,9 @@ int kvx_swap_blocks(kvx_layout* layout, int64_t num_entries,
     layout->L.host_pool_dev = layout->host.mapped ? layout->host.dev_base : 0;
   }
   std::lock_guard<std::mutex> g(st->mu);
+  if (grid)
+    return execute_grid_host(st, &gp, layout->host, layout->L.host_pool, mode,
+                             reinterpret_cast<cudaStream_t>(stream));
   return execute_host_copies(st, copies, is_swap_in != 0, layout->host, layout->L.host_pool,
                              mode, reinterpret_cast<cudaStream_t>(stream));
 }
@@ -820,13 +1078,22 @@ int kvx_migrate_blocks(kvx_layout* source, kvx_layout* target, int64_t num_entri
   if (!source || !target) return set_error(KVX_ERR_INVALID_ARGUMENT, "null layout");
   Entries e{num_entries, source_block_ids, target_block_ids, group_ids,
             first_kernel_blocks, valid_kernel_blocks};
+  GridPlan gp;
+  const bool grid = grid_migrate(source->L, target->L, e, &gp);
   std::vector<Copy> copies;
-  uint64_t copied = 0;
-  int rc = from_plan(plan_migrate(source->L, target->L, e, &copies, &copied));
-  if (rc) return rc;
+  uint64_t copied = 0, extents = 0;
+  int rc = KVX_OK;
+  if (grid) {
+    copied = gp.copied;
+    extents = gp.extents;
+  } else {
+    rc = from_plan(plan_migrate(source->L, target->L, e, &copies, &copied));
+    if (rc) return rc;
+    extents = copies.size();
+  }
   if (copied_bytes) *copied_bytes = copied;
-  if (copy_extents) *copy_extents = copies.size();
-  if (copies.empty()) {
+  if (copy_extents) *copy_extents = extents;
+  if (extents == 0) {
     t_last_mode = mode == KVX_MODE_AUTO ? KVX_MODE_SM : mode;
     return KVX_OK;
   }
@@ -851,15 +1118,19 @@ int kvx_migrate_blocks(kvx_layout* source, kvx_layout* target, int64_t num_entri
     }
   const Tunables tn = tunables();
   std::lock_guard<std::mutex> g(st->mu);
-  const std::vector<size_t> waves = split_waves(copies);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   if (mode == KVX_MODE_AUTO) mode = KVX_MODE_SM;
+  const Path path = local ? Path::kDevice : Path::kPeer;
   if (mode == KVX_MODE_CE || mode == KVX_MODE_CE_EXTENT) {
-    rc = run_ce_extent(copies, waves, s);
+    if (grid) copies = grid_copies(gp);
+    rc = run_ce_extent(copies, grid ? std::vector<size_t>{copies.size()} : split_waves(copies), s);
     mode = KVX_MODE_CE_EXTENT;
   } else if (mode == KVX_MODE_SM || mode == KVX_MODE_SM_BULK) {
     const bool bulk = mode == KVX_MODE_SM_BULK && local;
-    rc = run_sm(st, copies, waves, local ? Path::kDevice : Path::kPeer, bulk, s, tn);
+    if (grid)
+      rc = run_sm_grid(st, &gp, path, bulk, s, tn);
+    else
+      rc = run_sm(st, copies, split_waves(copies), path, bulk, s, tn);
     mode = bulk ? KVX_MODE_SM_BULK : KVX_MODE_SM;
   } else {
     return set_error(KVX_ERR_INVALID_ARGUMENT, "unknown transfer mode");

@@ -59,6 +59,10 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-migration", action="store_true")
+    p.add_argument("--migration-direction", choices=["pull", "push"], default="pull",
+                   help="pull: the decode rank copies from the prefill rank's mapped cache "
+                        "(the reference's decode-side migrate_blocks); push: the prefill "
+                        "rank stores into the decode rank's cache")
     return p.parse_args()
 
 
@@ -442,9 +446,11 @@ def cpu_baseline(seconds: float) -> dict:
                       f"2 GiB host cache, {threads} threads, {dt:.1f} s; cpu {cpu}"}
 
 
-def migration_bench(dist_, dev, steps: int, warmup: int) -> dict:
-    """Configuration 3 at N >= 2: pairs (i, i + N/2); the prefill rank pushes
-    its blocks into the decode rank's cache over NVLink."""
+def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull") -> dict:
+    """Configuration 3 at N >= 2: pairs (i, i + N/2), rank i the prefill side.
+    pull: the decode rank maps the prefill rank's cache and copies the blocks
+    in (loads over NVLink); push: the prefill rank stores them into the
+    decode rank's mapped cache."""
     import torch
 
     from aegaeon_b200 import swapper, workloads
@@ -466,14 +472,15 @@ def migration_bench(dist_, dev, steps: int, warmup: int) -> dict:
     pair = min(dist_.rank, partner)
     plan = workloads.migration_plan(sh, requests=8, seed=0, pair=pair)
     nbytes = plan.num_blocks * sh.composite_bytes
-    if is_src:
+    active = is_src if direction == "push" else not is_src
+    if active:
         sw.register_kvcache_mem_handles(partner, None, handles[partner])
     stream = torch.cuda.Stream(dev)
 
     def run():
-        if is_src:
+        if active:
             sw.migrate_blocks([pair], partner, plan.source_ids, plan.target_ids, None,
-                              direction="push", stream=stream)
+                              direction=direction, stream=stream)
 
     for _ in range(warmup):
         run()
@@ -487,17 +494,82 @@ def migration_bench(dist_, dev, steps: int, warmup: int) -> dict:
     b.synchronize()
     t = dist_.max(a.elapsed_time(b) / 1e3)
     dist_.barrier()
+    # Parity of the timed push: the decode rank's blocks equal the prefill
+    # rank's (checked on a digest of the moved pages, both sides on device).
+    moved = [p.view(-1, sh.page_bytes)[plan.source_ids if is_src else plan.target_ids]
+             for p in pages]
+    digest = torch.stack([m.view(torch.int32).sum(dtype=torch.int64) for m in moved]).cpu().tolist()
+    digests = dist_.gather_obj(digest)
+    parity = all(digests[r] == digests[r + half] for r in range(half))
+    del moved
+    nccl = nccl_comparison(dist_, dev, sw, plan, is_src, partner, steps, warmup)
     sw.close()
     del pages
     total = half * nbytes * steps
     per_pair = nbytes * steps / t / 1e9
     return {"config": "cfg3 Qwen2.5-7B P->D migration: 28 layers, 4 kv heads, 128 dim, bf16, "
                       "block 16; 8 requests/pair, prompts U{512..8192}; pairs (i, i+N/2); "
-                      "push over NVLink peer stores",
+                      f"{direction}: " + ("decode rank loads from the prefill rank's mapped "
+                                          "cache over NVLink" if direction == "pull" else
+                                          "prefill rank stores into the decode rank's mapped "
+                                          "cache over NVLink"),
             "pairs": half, "bytes_per_pair": nbytes, "value": total / t / 1e9, "unit": "GB/s",
             "per_pair_gbs": per_pair, "nvlink_peer_copy_gbs": 770.0,
             "frac_of_measured_peer_copy": per_pair / 770.0, "frac_of_nominal_900": per_pair / 900.0,
-            "ms_per_step": t / steps * 1e3}
+            "ms_per_step": t / steps * 1e3, "bit_exact": parity,
+            "nccl_sendrecv": {"value": half * nbytes / nccl / 1e9, "unit": "GB/s",
+                              "per_pair_gbs": nbytes / nccl / 1e9,
+                              "how": "gather blocks into a contiguous buffer (kvx kernel), "
+                                     "torch.distributed send/recv (NCCL), scatter on the "
+                                     "decode rank; CUDA events, max over ranks"}}
+
+
+def nccl_comparison(dist_, dev, sw, plan, is_src, partner, steps, warmup) -> float:
+    """Seconds per migration through NCCL send/recv of a gathered buffer."""
+    import torch
+    import torch.distributed as dist
+
+    from aegaeon_b200 import _lib, swapper
+
+    n = plan.num_blocks
+    segs = sw.segments
+    buf = torch.empty(n * sw.composite_page, dtype=torch.uint8, device=dev)
+    # segment-major staging: segment s holds the n moved pages back to back
+    staging_pages = [buf[i * n * s.page_size_bytes:(i + 1) * n * s.page_size_bytes]
+                     for i, s in enumerate(segs)]
+    st_segs, _ = swapper.make_segments([((f"st{i}",), n * s.page_size_bytes)
+                                        for i, s in enumerate(segs)], n)
+    staging = swapper.KVSwapper(dev.index, st_segs, staging_pages,
+                                [frozenset({0})] * len(segs), [1])
+    local, st_ep = sw.local_endpoint(), staging.local_endpoint()
+    cur = torch.cuda.current_stream(dev)
+    idx = list(range(n))
+
+    def move(src_ep, dst_ep, src_ids, dst_ids):
+        arr = swapper._entry_arrays(src_ids, dst_ids, [0] * n, [0] * n, [1] * n)
+        _lib.check(_lib.lib().kvx_migrate_blocks(src_ep.handle, dst_ep.handle, *arr,
+                                                 _lib.MODE_SM, cur.cuda_stream, None, None))
+
+    def once():
+        if is_src:
+            move(local, st_ep, plan.source_ids, idx)
+            dist.send(buf, dst=partner)
+        else:
+            dist.recv(buf, src=partner)
+            move(st_ep, local, idx, plan.target_ids)
+
+    for _ in range(warmup):
+        once()
+    dist_.barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(cur)
+    for _ in range(steps):
+        once()
+    b.record(cur)
+    b.synchronize()
+    t = dist_.max(a.elapsed_time(b) / 1e3)
+    staging.close()
+    return t / steps
 
 
 def traffic_from_profile() -> float | None:
@@ -528,7 +600,9 @@ def run_kvx(args):
             per_dir = max(64, rows_fit // 2 // 16 * 16)
     except (OSError, IndexError, ValueError):
         pass
+    dist_.barrier()  # every rank measures at once: the box's concurrent peak
     peaks = host_link_peaks(dev)
+    box_peak = dist_.sum(peaks["bidir_gbs"])
     per_dir = min(per_dir, args.cache_blocks // 2)
     bench = SwapBench(dev, per_dir, args.cache_blocks)
     lists = [bench.step_lists(k) for k in range(args.warmup + args.steps)]
@@ -564,7 +638,8 @@ def run_kvx(args):
     torch.cuda.empty_cache()
     mig = None
     if dist_.world >= 2 and not args.no_migration:
-        mig = migration_bench(dist_, dev, steps=args.steps, warmup=args.warmup)
+        mig = migration_bench(dist_, dev, steps=args.steps, warmup=args.warmup,
+                              direction=args.migration_direction)
     mp = measured_peaks()
     hbm_peak = mp.get("hbm_gbs", 6650.0)
     per_gpu = value / dist_.world
@@ -604,12 +679,14 @@ def run_kvx(args):
             "roofline": {
                 "bound": "host_link",
                 "achieved": per_gpu,
-                "peak": peaks["bidir_gbs"],
+                "peak": box_peak / dist_.world,
                 "unit": "GB/s",
-                "frac": per_gpu / peaks["bidir_gbs"],
+                "frac": value / box_peak,
                 "traffic": None,
                 "peak_source": "measured live: 1 GiB page-locked copy-engine copies H2D and "
-                               "D2H at once on this GPU (per GPU; the step is bidirectional)",
+                               "D2H at once, on every GPU of the run at the same time (per-GPU "
+                               "share of the box's concurrent peak; the step is bidirectional)",
+                "box_peak_gbs": box_peak,
                 "peak_h2d_gbs": peaks["h2d_gbs"],
                 "peak_d2h_gbs": peaks["d2h_gbs"],
                 "nominal_gbs_per_direction": 63.0,

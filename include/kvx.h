@@ -173,8 +173,11 @@ int kvx_byte_extent(uint64_t page_bytes, int64_t kernel_blocks_per_page,
 
 /* ---- planning introspection (host only, no GPU needed) ---------------------
  * Run the validation and planning of kvx_swap_blocks / kvx_swap without
- * touching a GPU and return the copies it would issue, in issue order, as
- * (source address, destination address, bytes) triples.  *num_copies_inout
+ * touching a GPU and return the copies the SM path would issue, as (source
+ * address, destination address, bytes) triples: when the request has a grid
+ * form (uniform pages, distinct targets, disjoint memory) these come from the
+ * same tile resolver the kernel uses, entry by entry; otherwise from the item
+ * planner in the reference's issue order (segment-major, then entries).  *num_copies_inout
  * holds the capacity of the three arrays on entry and the number of copies on
  * return (when the capacity is too small the arrays are left unfilled and
  * KVX_OK is returned with the required count).  Used by tests of the host
