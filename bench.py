@@ -51,6 +51,9 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["kvx", "reference"], default="kvx")
+    p.add_argument("--config", type=int, choices=[1, 2, 4, 5], default=2,
+                   help="BASELINE.json configuration (2 = the headline line; 3 is the "
+                        "migration object of the N>=2 line)")
     p.add_argument("--mode", default="auto", help="transfer mode: auto|sm|ce|ce_extent")
     p.add_argument("--blocks", type=int, default=1024, help="blocks per direction per step")
     p.add_argument("--cache-blocks", type=int, default=4096,
@@ -838,8 +841,263 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ---- configurations 1, 4 and 5 (one JSON line each, N=1 unless stated) ---------
+def _ref_module():
+    from oracle import build_ref
+
+    return build_ref.load_module()
+
+
+def _timed(stream_list, fn, steps, dev):
+    """Device time of `steps` calls of fn (which issues on the given streams)."""
+    import torch
+
+    cur = torch.cuda.current_stream(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(cur)
+    for st in stream_list:
+        st.wait_event(a)
+    for k in range(steps):
+        fn(k)
+    for st in stream_list:
+        cur.wait_stream(st)
+    b.record(cur)
+    b.synchronize()
+    return a.elapsed_time(b) / 1e3
+
+
+def run_config1(args):
+    """Qwen3-4B round trip through the per-tensor op: 72 tensors [1024,16,8,128]
+    bf16 N(0,1); 256 blocks out to slots 0..255, then back in to a fresh
+    permutation of a zeroed cache; bit-exact check of the round trip."""
+    import torch
+
+    from aegaeon_b200 import ops, workloads
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    sh = workloads.CFG1
+    gen = torch.Generator(device=dev).manual_seed(0)
+    shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+    caches = [torch.empty(shape, dtype=sh.dtype, device=dev).normal_(generator=gen)
+              for _ in range(sh.num_segments)]
+    back = [torch.zeros_like(c) for c in caches]
+    n = 256
+    hosts = [torch.empty((n,) + shape[1:], dtype=sh.dtype).pin_memory() for _ in caches]
+    out_ids = workloads.randperm(sh.num_blocks, 0)[:n]
+    in_ids = workloads.randperm(sh.num_blocks, 1)[:n]
+    slots = list(range(n))
+    ref = _ref_module() if args.impl == "reference" else None
+
+    def swap(src, dst, is_in, cache, host):
+        if ref is not None:
+            ref.swap(src, dst, is_in, cache, host)
+        else:
+            ops.swap(src, dst, is_in, cache, host, mode=args.mode)
+
+    def step(_k):
+        for c, h in zip(caches, hosts):
+            swap(out_ids, slots, False, c, h)
+        for c, h in zip(back, hosts):
+            swap(slots, in_ids, True, c, h)
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    t = _timed([], step, args.steps, dev)
+    wall = time.perf_counter() - t0
+    exact = all(torch.equal(b[in_ids].view(torch.uint8), c[out_ids].view(torch.uint8))
+                for b, c in zip(back, caches))
+    nbytes = 2 * sh.num_segments * n * sh.page_bytes * args.steps
+    value = nbytes / t / 1e9
+    return {"impl": args.impl, "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "dtype": "u8",
+            "config": {"workload": "cfg1 Qwen3-4B round trip: 36 layers x separate K/V "
+                                   "[1024,16,8,128] bf16 N(0,1) seed 0; 256 blocks out to "
+                                   "slots 0..255 then in to a fresh permutation, 72 swap "
+                                   "calls per direction",
+                       "api": "aegaeon.ops.swap (reference op)" if ref is not None
+                       else "aegaeon_b200.ops.swap -> kvx_swap",
+                       "transfer_mode": None if ref is not None else args.mode},
+            "bit_exact_round_trip": exact,
+            "e2e": {"value": nbytes / wall / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": nbytes // 2 // args.steps,
+                    "d2h_bytes_per_step": nbytes // 2 // args.steps}}
+
+
+def run_config4(args):
+    """Model-switch overlap: swap-in of 2048 cfg2 blocks (16 GiB) while a
+    Qwen1.5-14B TP-2 weight shard (14.17 GB bf16) is uploaded from
+    page-locked host memory in 64 MiB chunks on a second stream."""
+    import torch
+
+    from aegaeon_b200 import _lib, swapper, workloads
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    sh = workloads.CFG2
+    n = 2048
+    gen = torch.Generator(device=dev).manual_seed(0)
+    ws = workloads.WeightShard()
+    w_dev = torch.empty(ws.nbytes, dtype=torch.uint8, device=dev)
+    w_host = torch.empty(ws.nbytes, dtype=torch.uint8).pin_memory()
+    w_host[:: 1 << 20].fill_(1)
+    in_ids = workloads.randperm(sh.num_blocks, 7)[:n]
+    s_kv, s_w = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    ref = _ref_module() if args.impl == "reference" else None
+    if ref is None:
+        pages = [torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
+                 for _ in range(sh.num_segments)]
+        segs, comp = swapper.make_segments([((f"l{i}",), sh.num_blocks * sh.page_bytes)
+                                            for i in range(sh.num_segments)], sh.num_blocks)
+        pool = torch.empty(n * comp, dtype=torch.uint8).pin_memory()
+        pool[:: 1 << 20].fill_(2)
+        sw = swapper.KVSwapper(0, segs, pages, [frozenset({0})] * sh.num_segments, [1],
+                               kv_swap=pool)
+        rows = list(range(n))
+
+        def step(_k):
+            sw.swap_blocks([0], rows, in_ids, [0] * n, [0] * n, [1] * n, [None], True,
+                           mode=args.mode, stream=s_kv)
+            _lib.check(_lib.lib().kvx_upload_chunked(w_dev.data_ptr(), w_host.data_ptr(),
+                                                     ws.nbytes, 64 << 20, s_w.cuda_stream))
+    else:
+        shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+        caches = [torch.empty(shape, dtype=sh.dtype, device=dev) for _ in range(sh.num_segments)]
+        hosts = [torch.empty((n,) + shape[1:], dtype=sh.dtype).pin_memory() for _ in caches]
+        slots = list(range(n))
+        offs = [0]
+        for t in ws.tensors:
+            offs.append(offs[-1] + 2 * t)
+
+        def step(_k):
+            with torch.cuda.stream(s_kv):
+                for c, h in zip(caches, hosts):
+                    ref.swap(slots, in_ids, True, c, h)
+            with torch.cuda.stream(s_w):  # one copy per weight tensor (quick_loader.py:413)
+                for a, b in zip(offs[:-1], offs[1:]):
+                    w_dev[a:b].copy_(w_host[a:b], non_blocking=True)
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    t = _timed([s_kv, s_w], step, args.steps, dev)
+    wall = time.perf_counter() - t0
+    kv_bytes = n * sh.composite_bytes
+    per = t / args.steps
+    value = (kv_bytes + ws.nbytes) / per / 1e9
+    peaks = host_link_peaks(dev)
+    line = {"impl": args.impl, "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
+            "switch_ms": per * 1e3, "higher_is_better": True, "dtype": "u8",
+            "config": {"workload": "cfg4 switch overlap: swap-in of 2048 Llama-2-7B-shaped "
+                                   f"blocks ({kv_bytes} B) concurrent with a Qwen1.5-14B TP-2 "
+                                   f"bf16 weight shard ({ws.nbytes} B) uploaded on a second "
+                                   "stream",
+                       "weights": "64 MiB chunks, kvx_upload_chunked" if ref is None else
+                                  "one copy per weight tensor (quick_loader.py:413)"},
+            "roofline": {"bound": "host_link", "achieved": value, "peak": peaks["h2d_gbs"],
+                         "unit": "GB/s", "frac": value / peaks["h2d_gbs"],
+                         "peak_source": "measured live: 1 GiB page-locked H2D copy"},
+            "e2e": {"value": (kv_bytes + ws.nbytes) * args.steps / wall / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": kv_bytes + ws.nbytes, "d2h_bytes_per_step": 0}}
+    return line
+
+
+def run_config5(args):
+    """Fragmented swap-out: Qwen1.5-MoE shape (24 layers x K/V, 64 KiB pages),
+    16384 entries, half in contiguous device runs of 1..32 blocks, half
+    isolated; host slots sequential.  One call per step; per-call latency."""
+    import torch
+
+    from aegaeon_b200 import ops, swapper, workloads
+
+    dist_ = Dist.init(use_pg=args.impl == "kvx")
+    if args.impl == "reference" and dist_.rank != 0:
+        return None
+    dev = torch.device("cuda", dist_.local_rank)
+    sh = workloads.CFG5
+    n = 16384
+    avail = int([l for l in open("/proc/meminfo") if l.startswith("MemAvailable")][0].split()[1]) * 1024
+    fit = int(0.45 * avail / max(1, dist_.world if args.impl == "kvx" else 1) / sh.composite_bytes)
+    if fit < n:
+        n = max(1024, fit // 1024 * 1024)
+    ids, slots = workloads.fragmented_mapping(n, sh.num_blocks, seed=dist_.rank)
+    gen = torch.Generator(device=dev).manual_seed(dist_.rank)
+    ref = _ref_module() if args.impl == "reference" else None
+    s = torch.cuda.Stream(dev)
+    if ref is None:
+        pages = []
+        for _ in range(sh.num_segments):
+            t = torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
+            workloads.fill_segment(t, sh, gen)
+            pages.append(t)
+        segs, comp = swapper.make_segments([((f"l{i}",), sh.num_blocks * sh.page_bytes)
+                                            for i in range(sh.num_segments)], sh.num_blocks)
+        pool = torch.empty(n * comp, dtype=torch.uint8).pin_memory()
+        sw = swapper.KVSwapper(dev.index, segs, pages, [frozenset({0})] * sh.num_segments, [1],
+                               kv_swap=pool)
+
+        def step(_k):
+            sw.swap_blocks([0], ids, slots, [0] * n, [0] * n, [1] * n, [None], False,
+                           mode=args.mode, stream=s)
+    else:
+        shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+        caches = [torch.empty(shape, dtype=sh.dtype, device=dev).normal_(generator=gen)
+                  for _ in range(sh.num_segments)]
+        hosts = [torch.empty((n,) + shape[1:], dtype=sh.dtype).pin_memory() for _ in caches]
+
+        def step(_k):
+            with torch.cuda.stream(s):
+                for c, h in zip(caches, hosts):
+                    ref.swap(ids, slots, False, c, h)
+
+    for k in range(args.warmup):
+        step(k)
+    torch.cuda.synchronize()
+    dist_.barrier()
+    lat = []
+    t0 = time.perf_counter()
+    for k in range(args.steps):
+        lat.append(_timed([s], step, 1, dev))
+    wall = time.perf_counter() - t0
+    t = dist_.max(sum(lat))
+    nbytes = n * sh.composite_bytes
+    world = dist_.world if ref is None else 1
+    value = nbytes * args.steps * world / t / 1e9
+    line = None
+    if dist_.rank == 0:
+        line = {"impl": args.impl, "metric": METRIC, "value": value, "unit": "GB/s",
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": t / args.steps * 1e3, "call_latency_ms": sorted(x * 1e3 for x in lat),
+                "higher_is_better": True, "dtype": "u8", "scaling": "weak",
+                "config": {"workload": f"cfg5 Qwen1.5-MoE-A2.7B fragmented swap-out: 24 layers x "
+                                       f"K/V 64 KiB pages, {n} entries (half in contiguous "
+                                       "device runs of 1..32 blocks, half isolated), host "
+                                       "slots sequential; one call per step",
+                           "entries": n,
+                           "api": "KVSwapper.swap_blocks -> kvx_swap_blocks" if ref is None
+                           else "aegaeon.ops.swap (reference op), 48 calls per step"},
+                "e2e": {"value": nbytes * args.steps * world / wall / 1e9, "unit": "GB/s",
+                        "h2d_bytes_per_step": 0, "d2h_bytes_per_step": nbytes * world}}
+    dist_.finish()
+    return line
+
+
 def main():
     args = parse_args()
+    if args.config != 2:
+        rank = int(os.environ.get("RANK", "0"))
+        if args.config in (1, 4) and rank != 0:
+            return
+        fn = {1: run_config1, 4: run_config4, 5: run_config5}[args.config]
+        line = fn(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
