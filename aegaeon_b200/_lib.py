@@ -84,6 +84,7 @@ SIGNATURES = {
     "kvx_kernel_timing": (_int, [_int]),
     "kvx_kernel_timing_read": (_int, [_p_u64, ctypes.POINTER(ctypes.c_double), _p_u64]),
     "kvx_device_status": (_int, [_int, _int, ctypes.POINTER(_int)]),
+    "kvx_selftest_bounded_wait": (_int, [_u64, _vp]),
     "kvx_configure": (_int, [_i64, _i64, _i64, _i64]),
     "kvx_swap_noalloc": (_int, [_p_i64, _p_i64, _i64, _int, _vp, _u64, _u64, _vp, _u64, _vp]),
 }

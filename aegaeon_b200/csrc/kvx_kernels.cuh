@@ -149,13 +149,14 @@ __global__ void __launch_bounds__(kVecThreads)
 
 // ---- TMA bulk copy (local HBM only) ----------------------------------------
 
+// Device error word: set by kernels whose bounded waits gave up.
+static __device__ int g_kvx_device_status;
+
 constexpr int kBulkStages = 6;
 constexpr uint32_t kBulkShift = 14;
 constexpr uint32_t kBulkChunk = 1u << kBulkShift;  // one tile per stage
 constexpr uint32_t kBulkSmem = kBulkStages * kBulkChunk + kBulkStages * 8;
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s per wait
-
-static __device__ int g_kvx_device_status;
 
 __device__ __forceinline__ uint64_t global_ns() {
   uint64_t t;
@@ -176,12 +177,28 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
 }
 
 // Bounded wait; false when the deadline passed.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __forceinline__ bool mbar_wait_for(uint32_t bar, uint32_t parity, uint64_t limit_ns) {
   if (mbar_try(bar, parity)) return true;
   const uint64_t start = global_ns();
   while (!mbar_try(bar, parity))
-    if (global_ns() - start > kWaitLimitNs) return false;
+    if (global_ns() - start > limit_ns) return false;
   return true;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  return mbar_wait_for(bar, parity, kWaitLimitNs);
+}
+
+// Self-test of the bounded wait: waits on an mbarrier that nothing arrives on;
+// the wait gives up after limit_ns and the kernel records the timeout in the
+// device status word, exactly as the copy kernel does.
+static __global__ void __launch_bounds__(32) kvx_wait_selftest(uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x != 0) return;
+  const uint32_t b = static_cast<uint32_t>(__cvta_generic_to_shared(&bar));
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(b) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  if (!mbar_wait_for(b, 0, limit_ns)) atomicExch(&g_kvx_device_status, 8 /* timeout */);
 }
 
 __device__ __forceinline__ void bulk_load(uint32_t smem, const void* src,

@@ -1227,6 +1227,15 @@ int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,
   return KVX_OK;
 }
 
+int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream) {
+  t_last_error.clear();
+  if (limit_ns == 0 || limit_ns > 10ull * 1000 * 1000 * 1000)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 10 s]");
+  kvx_wait_selftest<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(limit_ns);
+  KVX_CUDA(cudaGetLastError());
+  return KVX_OK;
+}
+
 int kvx_device_status(int device, int reset, int* status_out) {
   t_last_error.clear();
   if (!status_out) return set_error(KVX_ERR_INVALID_ARGUMENT, "null status_out");

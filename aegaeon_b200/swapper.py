@@ -387,7 +387,8 @@ class KVSwapper:
                        first_kernel_blocks: Optional[Sequence[int]] = None,
                        valid_kernel_blocks: Optional[Sequence[int]] = None,
                        *, direction: str = "pull", mode: str | int = "auto",
-                       stream: Optional[torch.cuda.Stream] = None) -> torch.cuda.Event:
+                       stream: Optional[torch.cuda.Stream] = None,
+                       liveness=None) -> torch.cuda.Event:
         """Copy blocks between this GPU and a registered peer over NVLink.
 
         ``direction="pull"`` (the reference's decode-side signature): the peer
@@ -395,7 +396,12 @@ class KVSwapper:
         them at ``target_block_ids``.  ``direction="push"``: this cache is the
         source and the registered peer ``source_engine_id`` the target.
         Without group / extent lists every entry is a full page of group 0.
+        ``liveness`` (e.g. ``Heartbeat.guard(peer)``) is called before anything
+        is queued and raises when the peer process has gone, so no copy ever
+        touches the memory of a departed peer.
         """
+        if liveness is not None:
+            liveness()
         if source_engine_id not in self._peers:
             raise ValueError(f"no KV-cache handles registered for engine {source_engine_id}")
         n = len(source_block_ids)

@@ -216,6 +216,14 @@ int kvx_kernel_timing_read(uint64_t* launches, double* total_ms,
                            uint64_t* hbm_bytes);
 int kvx_device_status(int device, int reset, int* status_out);
 
+/* Self-test of the device-side timeout path: launches, on `stream`, a kernel
+ * that waits (with the same bounded mbarrier wait the TMA copy kernel uses) on
+ * a barrier nothing arrives on.  After limit_ns the wait gives up and the
+ * kernel sets the device status word to KVX_ERR_DEVICE_TIMEOUT, which
+ * kvx_device_status then reports; the context stays usable.  No counterpart
+ * in the reference (it has no device-side waits). */
+int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream);
+
 /* Tuning knobs of KVX_MODE_AUTO and of the kernels; 0 keeps the current value.
  *   sm_ctas_host : CTAs of an SM kernel that touches host memory
  *   sm_ctas_dev  : CTAs of an SM kernel that touches device memory only

@@ -1,0 +1,42 @@
+"""Device-side failure handling without a GPU fault.
+
+The only device-side waits of the library are the TMA copy kernel's mbarrier
+waits, each bounded by a deadline.  kvx_selftest_bounded_wait runs that same
+wait on a barrier nothing arrives on: it must give up after its limit, record
+KVX_ERR_DEVICE_TIMEOUT in the device status word, and leave the context
+usable for the next copies.
+"""
+
+import time
+
+import pytest
+import torch
+
+from aegaeon_b200 import _lib, ops
+
+pytestmark = pytest.mark.gpu
+
+
+def test_bounded_wait_gives_up_and_reports(cuda):
+    lib = _lib.lib()
+    assert _lib.device_status(0, reset=True) in (0, _lib.KVX_ERR_DEVICE_TIMEOUT)
+    s = torch.cuda.current_stream()
+    t0 = time.perf_counter()
+    _lib.check(lib.kvx_selftest_bounded_wait(50_000_000, s.cuda_stream))  # 50 ms
+    assert _lib.device_status(0) == _lib.KVX_ERR_DEVICE_TIMEOUT
+    assert time.perf_counter() - t0 < 5.0
+    assert _lib.device_status(0, reset=True) == _lib.KVX_ERR_DEVICE_TIMEOUT
+    assert _lib.device_status(0) == 0
+    # the context is still usable
+    cache = torch.randn((16, 16, 8, 128), device=cuda).to(torch.bfloat16)
+    host = torch.zeros((16, 16, 8, 128), dtype=torch.bfloat16).pin_memory()
+    ops.swap(list(range(16)), list(range(16)), False, cache, host)
+    torch.cuda.synchronize()
+    assert torch.equal(host.view(torch.uint8), cache.cpu().view(torch.uint8))
+    assert _lib.device_status(0) == 0
+
+
+def test_selftest_rejects_bad_limits(cuda):
+    lib = _lib.lib()
+    assert lib.kvx_selftest_bounded_wait(0, None) == _lib.KVX_ERR_INVALID_ARGUMENT
+    assert lib.kvx_selftest_bounded_wait(11 * 10**9, None) == _lib.KVX_ERR_INVALID_ARGUMENT

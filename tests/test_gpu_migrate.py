@@ -3,6 +3,7 @@ worker.py:2420-2451): same-GPU copies through both kernels, and, with two
 GPUs, pull and push over IPC-mapped peer memory."""
 
 import os
+import time
 
 import numpy as np
 import pytest
@@ -152,3 +153,86 @@ def test_two_gpu_migration(cuda, direction):
     for e, b in zip(exp, got):
         assert e.tobytes() == b
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _liveness_worker(rank, port, q_out, q_in, page, blocks, layers):
+    """rank 0 = prefill (exports, beats, departs between steps);
+    rank 1 = decode (pulls while rank 0 is there, then must refuse)."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from aegaeon_b200.liveness import Heartbeat, PeerGone
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    store = dist.TCPStore("127.0.0.1", port, 2, rank == 1, timeout=datetime.timedelta(seconds=60))
+    hb = Heartbeat(store, rank, interval=0.05)
+    pages = cache_pages(dev, layers, blocks, page, 200 + rank)
+    sw = make(rank, page, pages)
+    q_out.put(("handles", sw.export_kvcache_mem_handles()))
+    if rank == 0:
+        q_in.get(timeout=120)  # the decode side finished its pull: leave now
+        torch.cuda.synchronize()
+        hb.depart()            # announced before the memory goes away
+        q_out.put(("left", None))
+        q_out.close()
+        q_out.join_thread()
+        os._exit(0)
+    handles = q_in.get(timeout=120)[1]
+    sw.register_kvcache_mem_handles(0, None, handles)
+    sid, did = list(range(64)), list(range(64, 128))
+    sw.migrate_blocks([0], 0, sid, did, None, liveness=hb.guard(0, max_age=2.0)).synchronize()
+    expect = cache_pages(torch.device("cuda", 0), 1, blocks, page, 200)[0].view(-1, page)[0:64]
+    ok_first = torch.equal(pages[0].view(-1, page)[64:128].cpu(), expect.cpu())
+    sw.unregister_kvcache_mem_handles(0)  # unmap the peer before it may go away
+    q_out.put(("first", ok_first))
+    q_in.get(timeout=120)  # the prefill process has departed and exited
+    refused = None
+    try:
+        sw.migrate_blocks([0], 0, sid, did, None, liveness=hb.guard(0, max_age=2.0))
+    except PeerGone as e:
+        refused = str(e)
+    q_out.put(("refused", refused))
+    q_out.close()
+    q_out.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.multigpu
+def test_departed_prefill_peer_is_never_read(cuda):
+    """The decode worker checks the prefill worker's liveness before each
+    pull.  Once the prefill process has departed (between steps, nothing in
+    flight) the next pull is refused on the host: nothing reads the departed
+    peer's memory.  (Silent deaths, found by heartbeat age, are tested on CPU
+    ranks in test_liveness_gloo.py.)"""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    ctx = mp.get_context("spawn")
+    q0, q1, qa, qb = ctx.Queue(), ctx.Queue(), ctx.Queue(), ctx.Queue()
+    port = 29700 + os.getpid() % 1000
+    procs = [ctx.Process(target=_liveness_worker, args=(0, port, q0, qa, 16384, 256, 2)),
+             ctx.Process(target=_liveness_worker, args=(1, port, q1, qb, 16384, 256, 2))]
+    for p in procs:
+        p.start()
+    try:
+        h0 = q0.get(timeout=180)
+        q1.get(timeout=180)
+        qb.put(h0)
+        first = q1.get(timeout=180)
+        qa.put("leave")
+        assert q0.get(timeout=180)[0] == "left"
+        procs[0].join(timeout=120)
+        assert not procs[0].is_alive()
+        qb.put("go")
+        refused = q1.get(timeout=180)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert first == ("first", True)
+    assert refused[0] == "refused" and refused[1] is not None and "left" in refused[1]
