@@ -85,7 +85,7 @@ SIGNATURES = {
     "kvx_kernel_timing_read": (_int, [_p_u64, ctypes.POINTER(ctypes.c_double), _p_u64]),
     "kvx_device_status": (_int, [_int, _int, ctypes.POINTER(_int)]),
     "kvx_selftest_bounded_wait": (_int, [_u64, _vp]),
-    "kvx_configure": (_int, [_i64, _i64, _i64, _i64]),
+    "kvx_configure": (_int, [_i64, _i64, _i64, _i64, _i64]),
     "kvx_swap_noalloc": (_int, [_p_i64, _p_i64, _i64, _int, _vp, _u64, _u64, _vp, _u64, _vp]),
 }
 
@@ -170,10 +170,12 @@ def last_mode_name() -> str:
 
 
 def configure(sm_ctas_host: int = 0, sm_ctas_dev: int = 0, ce_min_run: int = 0,
-              staging_bytes: int = 0) -> None:
+              staging_bytes: int = 0, ce_pipeline: int = -1) -> None:
     """Set the tuning knobs of the transfer-mode policy (0 keeps a value;
-    ce_min_run < 0 disables the copy-engine choice of the AUTO mode)."""
-    check(lib().kvx_configure(sm_ctas_host, sm_ctas_dev, ce_min_run, staging_bytes))
+    ce_min_run < 0 disables the copy-engine choice of the AUTO mode;
+    ce_pipeline: -1 keeps, 0 off, 1 double-buffered staging)."""
+    check(lib().kvx_configure(sm_ctas_host, sm_ctas_dev, ce_min_run, staging_bytes,
+                              ce_pipeline))
 
 
 def device_status(device: int, reset: bool = False) -> int:

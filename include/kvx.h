@@ -224,13 +224,20 @@ int kvx_device_status(int device, int reset, int* status_out);
  * in the reference (it has no device-side waits). */
 int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream);
 
-/* Tuning knobs of KVX_MODE_AUTO and of the kernels; 0 keeps the current value.
+/* Tuning knobs of KVX_MODE_AUTO and of the kernels; 0 keeps the current value
+ * (ce_pipeline: -1 keeps it).
  *   sm_ctas_host : CTAs of an SM kernel that touches host memory
  *   sm_ctas_dev  : CTAs of an SM kernel that touches device memory only
  *   ce_min_run   : mean coalesced host-run bytes from which AUTO uses the CE
- *   staging_bytes: size of each staging area of the copy-engine mode        */
+ *   staging_bytes: size of each staging area of the copy-engine mode
+ *                  (one per direction and device, 256 MiB by default)
+ * Environment: KVX_SM_CTAS_HOST, KVX_SM_CTAS_DEV, KVX_CE_MIN_RUN,
+ * KVX_STAGING_BYTES, and KVX_CE_PIPELINE=1 to double-buffer the staging area
+ * (gather/scatter of one half on an internal stream while the copy engines
+ * move the other; helps a single direction, hurts concurrent directions). */
 int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
-                  int64_t ce_min_run, int64_t staging_bytes);
+                  int64_t ce_min_run, int64_t staging_bytes,
+                  int64_t ce_pipeline /* -1 keep, 0 off, 1 on */);
 
 /* ---- allocation-free swap ---------------------------------------------------
  * No counterpart in the reference.  For callers that must not allocate GPU

@@ -206,5 +206,38 @@ def test_swap_blocks_events_order_moves(cuda):
     sw.close()
 
 
+@pytest.mark.parametrize("pipeline", [0, 1])
+def test_staged_chunks_parity(cuda, oracle, pipeline):
+    """Copy-engine mode over many staging chunks (small staging area), with
+    and without the double-buffered pipeline: bytes equal the oracle's."""
+    pages = [65536] * 6
+    nb, rows = 96, 80
+    segs = [torch.randint(0, 255, (nb * p,), dtype=torch.uint8, device=cuda) for p in pages]
+    segments, comp = swapper.make_segments([((f"l{i}",), nb * p) for i, p in enumerate(pages)], nb)
+    pool = torch.randint(0, 255, (rows * comp,), dtype=torch.uint8).pin_memory()
+    sw = swapper.KVSwapper(0, segments, segs, [frozenset({0})] * 6, [1], kv_swap=pool)
+    _lib.configure(staging_bytes=4 << 20, ce_pipeline=pipeline)
+    try:
+        g = torch.Generator().manual_seed(30 + pipeline)
+        dev_ids = torch.randperm(nb, generator=g)[:70].tolist()
+        host_ids = torch.randperm(rows, generator=g)[:70].tolist()
+        n = 70
+        for is_in in (False, True):
+            exp_pool = pool.numpy().copy()
+            exp_segs = [t.cpu().numpy().copy() for t in segs]
+            src, dst = (host_ids, dev_ids) if is_in else (dev_ids, host_ids)
+            oracle.swap_blocks(exp_segs, pages, [s.cpu_offset for s in segments], [1] * 6, [1],
+                               exp_pool, comp, 0, src, dst, [0] * n, [0] * n, [1] * n, is_in)
+            sw.swap_blocks([0], src, dst, [0] * n, [0] * n, [1] * n, [None], is_in,
+                           mode="ce").synchronize()
+            assert np.array_equal(pool.numpy(), exp_pool)
+            for t, e in zip(segs, exp_segs):
+                assert np.array_equal(t.cpu().numpy(), e)
+            host_ids = torch.randperm(rows, generator=g)[:70].tolist()
+    finally:
+        _lib.configure(staging_bytes=256 << 20, ce_pipeline=0)
+        sw.close()
+
+
 def test_device_status_clean(cuda):
     assert _lib.device_status(0) == 0
