@@ -25,6 +25,8 @@ KVX_ERR_CUDA = 7
 KVX_ERR_DEVICE_TIMEOUT = 8
 KVX_ERR_LAYOUT = 9
 KVX_ERR_NO_MEMORY = 10
+KVX_ERR_IO = 11
+KVX_ERR_FORMAT = 12
 
 MODE_AUTO = 0
 MODE_SM = 1
@@ -87,6 +89,7 @@ SIGNATURES = {
     "kvx_selftest_bounded_wait": (_int, [_u64, _vp]),
     "kvx_configure": (_int, [_i64, _i64, _i64, _i64, _i64]),
     "kvx_swap_noalloc": (_int, [_p_i64, _p_i64, _i64, _int, _vp, _u64, _u64, _vp, _u64, _vp]),
+    "kvx_safetensors_meta_json": (_int, [ctypes.c_char_p, ctypes.c_char_p, _u64, _p_u64]),
 }
 
 _lock = threading.Lock()

@@ -18,9 +18,11 @@ SOURCES = [
     os.path.join(HERE, "csrc", "kvx_plan.cpp"),
     os.path.join(HERE, "csrc", "kvx_runtime.cu"),
     os.path.join(HERE, "csrc", "kvx_noalloc.cu"),
+    os.path.join(HERE, "csrc", "kvx_safetensors.cpp"),
 ]
 HEADERS = [
     os.path.join(HERE, "csrc", "kvx_plan.h"),
+    os.path.join(HERE, "csrc", "kvx_worklist.h"),
     os.path.join(HERE, "csrc", "kvx_kernels.cuh"),
     os.path.join(ROOT, "include", "kvx.h"),
 ]

@@ -869,6 +869,8 @@ const char* kvx_status_string(int status) {
     case KVX_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
     case KVX_ERR_LAYOUT: return "layouts differ";
     case KVX_ERR_NO_MEMORY: return "out of memory";
+    case KVX_ERR_IO: return "file cannot be read";
+    case KVX_ERR_FORMAT: return "invalid file format";
     default: return "unknown status";
   }
 }

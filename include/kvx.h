@@ -47,6 +47,8 @@ extern "C" {
 #define KVX_ERR_DEVICE_TIMEOUT 8   /* a bounded device-side wait gave up       */
 #define KVX_ERR_LAYOUT 9           /* the two layouts of a migration differ    */
 #define KVX_ERR_NO_MEMORY 10       /* a library work area could not be made    */
+#define KVX_ERR_IO 11              /* a file could not be opened or read       */
+#define KVX_ERR_FORMAT 12          /* a file is not valid in its format        */
 
 /* ---- transfer modes (the `mode` argument of the copy entry points) ------- */
 #define KVX_MODE_AUTO 0     /* per-call choice by size and fragmentation       */
@@ -238,6 +240,19 @@ int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream);
 int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
                   int64_t ce_min_run, int64_t staging_bytes,
                   int64_t ce_pipeline /* -1 keep, 0 off, 1 on */);
+
+/* ---- (f4) safetensors header ------------------------------------------------
+ * Reads the header of a .safetensors file and validates it as the
+ * `safetensors` crate 0.4.3 does (SafeTensors::read_metadata): header length,
+ * UTF-8 JSON, dtypes, offsets tiling the data without gaps, sizes equal to
+ * shape x dtype, nothing after the last tensor.  Writes the JSON the reference
+ * returns (file_path, size, offset = 8 + header length, tensor_info_map of
+ * dtype / shape / data_offsets) into `out` (NUL-terminated) when `capacity`
+ * exceeds its length; *length_out always receives the length.
+ * Errors: KVX_ERR_IO (cannot open/read), KVX_ERR_FORMAT (invalid header).
+ * Replaces: read_safetensors_meta_as_json, quick_model_loader/rsrc/lib.rs:19-51. */
+int kvx_safetensors_meta_json(const char* file_path, char* out,
+                              uint64_t capacity, uint64_t* length_out);
 
 /* ---- allocation-free swap ---------------------------------------------------
  * No counterpart in the reference.  For callers that must not allocate GPU
