@@ -71,6 +71,15 @@ SIGNATURES = {
     "kvx_ipc_export": (_int, [_vp, ctypes.POINTER(ctypes.c_uint8), _p_u64]),
     "kvx_ipc_import": (_int, [_int, ctypes.POINTER(ctypes.c_uint8), _u64, ctypes.POINTER(_vp)]),
     "kvx_ipc_close": (_int, [_int, _vp]),
+    "kvx_event_create": (_int, [_int, ctypes.POINTER(_vp)]),
+    "kvx_event_record": (_int, [_vp, _vp]),
+    "kvx_event_query": (_int, [_vp, ctypes.POINTER(_int)]),
+    "kvx_event_synchronize": (_int, [_vp]),
+    "kvx_event_ipc_handle": (_int, [_vp, ctypes.POINTER(ctypes.c_uint8)]),
+    "kvx_event_open_ipc": (_int, [ctypes.POINTER(ctypes.c_uint8), ctypes.POINTER(_vp)]),
+    "kvx_event_forget_ipc": (_int, [ctypes.POINTER(ctypes.c_uint8)]),
+    "kvx_stream_wait_events": (_int, [_vp, ctypes.POINTER(_vp), _i64]),
+    "kvx_event_release": (_int, [_vp]),
     "kvx_upload_chunked": (_int, [_vp, _vp, _u64, _u64, _vp]),
     "kvx_byte_extent": (_int, [_u64, _i64, _i64, _i64, _p_u64, _p_u64]),
     "kvx_plan_swap_blocks": (

@@ -19,6 +19,7 @@ SOURCES = [
     os.path.join(HERE, "csrc", "kvx_runtime.cu"),
     os.path.join(HERE, "csrc", "kvx_noalloc.cu"),
     os.path.join(HERE, "csrc", "kvx_safetensors.cpp"),
+    os.path.join(HERE, "csrc", "kvx_events.cu"),
 ]
 HEADERS = [
     os.path.join(HERE, "csrc", "kvx_plan.h"),

@@ -239,13 +239,15 @@ class KVSwapper:
                     first_kernel_blocks: Sequence[int], valid_kernel_blocks: Sequence[int],
                     source_events: Sequence[Optional[torch.cuda.Event]], is_swap_in: bool,
                     *, mode: str | int = "auto", stream: Optional[torch.cuda.Stream] = None,
-                    interprocess: bool = False) -> torch.cuda.Event:
+                    interprocess: bool = False, return_handle: bool = False):
         """Swap the live extents of blocks between GPU pages and host rows.
 
         Queued on the swap-in / swap-out stream after the given source events
-        (None entries wait for nothing) and returns an event recorded after
-        the copies.  ``copied_bytes`` / ``copy_extents`` of the call are left
-        in ``last_stats``.
+        (see ``_wait_source_events``) and returns an event recorded after the
+        copies; with ``return_handle`` it returns ``(device, handle bytes)`` of
+        an interprocess event instead, the reference's return value
+        (worker.py:2349).  ``copied_bytes`` / ``copy_extents`` of the call are
+        left in ``last_stats``.
         """
         if self.kv_swap_view is None:
             raise ValueError("this KVSwapper has no host pool")
@@ -254,8 +256,14 @@ class KVSwapper:
             valid_kernel_blocks)
         if stream is None:
             stream = self.swap_in_stream if is_swap_in else self.swap_out_stream
-        new_event = torch.cuda.Event(interprocess=interprocess)
-        self._wait_source_events(stream, new_event, request_ids, source_events)
+        with torch.cuda.device(self.device):
+            if return_handle:
+                from . import events as kev
+
+                new_event = kev.Event(interprocess=True)
+            else:
+                new_event = torch.cuda.Event(interprocess=interprocess)
+            self._wait_source_events(stream, new_event, request_ids, source_events)
         copied = ctypes.c_uint64(0)
         extents = ctypes.c_uint64(0)
         with torch.cuda.device(self.device):
@@ -275,6 +283,11 @@ class KVSwapper:
             copied.value, full, 0.0 if full == 0 else 100.0 * (1 - copied.value / full),
             extents.value,
         )
+        if return_handle:
+            from . import events as kev
+
+            with torch.cuda.device(self.device):
+                return kev.reduce_event(new_event)
         return new_event
 
     def plan_swap_blocks(self, source_block_ids, target_block_ids, group_ids,
@@ -299,14 +312,36 @@ class KVSwapper:
 
     def _wait_source_events(self, stream, new_event, request_ids, source_events):
         """Order this move after earlier moves of the same requests
-        (worker.py:2351-2394, with torch events instead of Ray-shipped IPC
-        handles)."""
+        (worker.py:2351-2394).  An entry may be None (nothing to wait for), a
+        torch or kvx event, or a ``(device, handle bytes)`` pair as produced
+        by ``swap_blocks(..., return_handle=True)`` in any worker (the
+        reference's ``reduce_cuda_event`` format).  A handle exported on this
+        device stands for the request's latest local event, as in the
+        reference; other handles are opened once and cached natively, and all
+        kvx events are waited on in one call."""
+        from . import events as kev
+
         if source_events is None:
             source_events = [None] * len(request_ids)
+        batch = []
         for request_id, ev in zip(request_ids, source_events):
             if ev is not None:
-                stream.wait_event(ev)
+                if isinstance(ev, tuple):
+                    opened = kev.rebuild_event(ev, is_worker=True)
+                    if opened is None:
+                        if not self.move_event_table.get(request_id):
+                            raise ValueError(
+                                f"request {request_id} should have a local event here")
+                        ev = self.move_event_table[request_id][-1]
+                    else:
+                        ev = opened
+                if isinstance(ev, kev.Event):
+                    batch.append(ev)
+                else:
+                    stream.wait_event(ev)
             self.move_event_table[request_id].append(new_event)
+        if batch:
+            kev.stream_wait(stream, batch)
 
     def clear_request_resource(self, request_id: int) -> None:
         self.move_event_table.pop(request_id, None)

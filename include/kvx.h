@@ -157,6 +157,29 @@ int kvx_ipc_import(int device, const uint8_t* handle64, uint64_t offset,
                    void** dev_ptr_out);
 int kvx_ipc_close(int device, void* dev_ptr);
 
+/* ---- (f3) events ordering moves across workers -------------------------------
+ * Pooled CUDA events, interprocess handles, and a cache of opened handles.
+ * Replaces the per-call cudaIpcOpenEventHandle / cudaStreamWaitEvent /
+ * cudaEventDestroy of Worker._wait_source_events (aegaeon/worker.py:2351-2394,
+ * utils.py:263-288).  create: an event of the current device from the pool
+ * (interprocess != 0: shareable).  query: *done = 1 once its last record has
+ * completed.  ipc_handle: 64 bytes for another process.  open_ipc: the event
+ * behind a handle, opened once and cached by the handle bytes (release drops
+ * the reference, the cache keeps the event; forget_ipc closes it).
+ * stream_wait_events: `stream` waits for every event of the list.  release:
+ * back to the pool (an interprocess event whose handle was shared must not be
+ * released while another process may still wait on that record). */
+typedef struct kvx_event kvx_event;
+int kvx_event_create(int interprocess, kvx_event** out);
+int kvx_event_record(kvx_event* event, void* stream);
+int kvx_event_query(kvx_event* event, int* done);
+int kvx_event_synchronize(kvx_event* event);
+int kvx_event_ipc_handle(kvx_event* event, uint8_t* handle_out64);
+int kvx_event_open_ipc(const uint8_t* handle64, kvx_event** out);
+int kvx_event_forget_ipc(const uint8_t* handle64);
+int kvx_stream_wait_events(void* stream, kvx_event* const* events, int64_t n);
+int kvx_event_release(kvx_event* event);
+
 /* ---- (f1) chunked weight upload for a model switch --------------------------
  * Host -> device copy of `bytes` bytes issued as copy-engine copies of at most
  * chunk_bytes each on `stream` (64 MiB chunks in the switch pipeline).

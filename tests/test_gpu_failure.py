@@ -40,3 +40,32 @@ def test_selftest_rejects_bad_limits(cuda):
     lib = _lib.lib()
     assert lib.kvx_selftest_bounded_wait(0, None) == _lib.KVX_ERR_INVALID_ARGUMENT
     assert lib.kvx_selftest_bounded_wait(11 * 10**9, None) == _lib.KVX_ERR_INVALID_ARGUMENT
+
+
+def test_native_events_local(cuda):
+    """Pool events record/query/synchronize; a handle exported on this device
+    rebuilds to None (the caller then uses its local event)."""
+    from aegaeon_b200 import events as kev
+
+    s = torch.cuda.Stream(cuda)
+    ev = kev.Event(interprocess=True)
+    x = torch.randn(4096, 4096, device=cuda)
+    with torch.cuda.stream(s):
+        y = x @ x
+    ev.record(s)
+    ev.synchronize()
+    assert ev.query()
+    h = kev.reduce_event(ev)
+    assert h[0] == torch.cuda.current_device() and len(h[1]) == 64
+    assert kev.rebuild_event(h) is None
+    s2 = torch.cuda.Stream(cuda)
+    kev.stream_wait(s2, [ev])
+    with torch.cuda.stream(s2):
+        z = y.sum()
+    torch.cuda.synchronize()
+    assert torch.isfinite(z)
+    handle = ev.handle
+    ev.release()
+    again = kev.Event(interprocess=True)
+    assert again.handle == handle  # reused from the pool
+    again.release()

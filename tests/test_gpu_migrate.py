@@ -236,3 +236,74 @@ def test_departed_prefill_peer_is_never_read(cuda):
                 p.kill()
     assert first == ("first", True)
     assert refused[0] == "refused" and refused[1] is not None and "left" in refused[1]
+
+
+def _ipc_event_worker(rank, q_out, q_in):
+    """rank 0 swaps host data into its cache and ships the (device, handle)
+    of the swap's interprocess event at once; rank 1 pulls those blocks after
+    waiting on that event."""
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    page, blocks, layers = 262144, 256, 8
+    pages = [torch.zeros(blocks * page, dtype=torch.uint8, device=dev) for _ in range(layers)]
+    segs, comp = swapper.make_segments([((f"l{i}",), blocks * page) for i in range(layers)], blocks)
+    pool = torch.full((blocks * comp,), 0x5A, dtype=torch.uint8).pin_memory() if rank == 0 else None
+    sw = swapper.KVSwapper(rank, segs, pages, [frozenset({0})] * layers, [1], kv_swap=pool)
+    q_out.put(("handles", sw.export_kvcache_mem_handles()))
+    if rank == 0:
+        q_in.get(timeout=120)
+        ids = list(range(blocks))
+        handle = sw.swap_blocks([1], ids, ids, [0] * blocks, [0] * blocks, [1] * blocks, [None],
+                                True, return_handle=True)
+        q_out.put(("event", handle))  # before the swap-in has finished
+        q_in.get(timeout=120)
+        torch.cuda.synchronize()
+        q_out.put(("bye", None))
+        q_out.close()
+        q_out.join_thread()
+        os._exit(0)
+    handles = q_in.get(timeout=120)[1]
+    sw.register_kvcache_mem_handles(0, None, handles)
+    handle = q_in.get(timeout=120)[1]
+    ids = list(range(blocks))
+    sw.migrate_blocks([1], 0, ids, ids, [handle]).synchronize()
+    ok = all(bool((p == 0x5A).all()) for p in pages)
+    sw.unregister_kvcache_mem_handles(0)
+    q_out.put(("result", ok))
+    q_out.close()
+    q_out.join_thread()
+    os._exit(0)
+
+
+@pytest.mark.multigpu
+def test_pull_waits_on_producer_ipc_event(cuda):
+    """Cross-process ordering with the native event layer: the decode worker
+    pulls blocks the prefill worker is still swapping in, after waiting on
+    the prefill swap's interprocess event (the reference's reduce/rebuild
+    handle format); it must see the swapped-in bytes."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q0, q1, qa, qb = ctx.Queue(), ctx.Queue(), ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_ipc_event_worker, args=(0, q0, qa)),
+             ctx.Process(target=_ipc_event_worker, args=(1, q1, qb))]
+    for p in procs:
+        p.start()
+    try:
+        h0 = q0.get(timeout=180)
+        q1.get(timeout=180)
+        qb.put(h0)
+        qa.put("go")
+        ev = q0.get(timeout=180)
+        qb.put(ev)
+        result = q1.get(timeout=180)
+        qa.put("done")
+        assert q0.get(timeout=180)[0] == "bye"
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert result == ("result", True)
