@@ -43,6 +43,13 @@ sys.path.insert(0, ROOT)
 
 METRIC = "KV swap GB/s per GPU & box (1/2/4/8) vs host-link/NVLink roofline; switch ms"
 GIB = 1 << 30
+_OUT = sys.stdout
+
+
+def emit(line: dict) -> None:
+    """Print the result line on the real stdout."""
+    _OUT.write(json.dumps(line) + "\n")
+    _OUT.flush()
 
 
 def parse_args():
@@ -209,13 +216,17 @@ def measured_peaks() -> dict:
         return {}
 
 
-def host_link_peaks(dev) -> dict:
-    """Copy-engine peaks of this GPU's host link: 2 GiB of page-locked memory
-    per direction copied as 256 MiB pieces back to back (single multi-GiB
-    copies run slower on this link), in each direction and in both at once;
-    best of 5 after a warm-up pass, CUDA events."""
+def host_link_peaks(dev, dist_=None) -> dict:
+    """Copy-engine peaks of the host links of all GPUs of the run together:
+    every rank copies 2 GiB of page-locked memory per direction as 256 MiB
+    pieces back to back (single multi-GiB copies run slower on this link),
+    H2D alone, D2H alone, and both at once.  All ranks start each window after
+    a barrier; a window's box figure is (bytes of all ranks) / (slowest
+    rank's device time).  Best of 5 windows after a warm-up; values returned
+    per GPU (box / N) plus the box figure of both directions."""
     import torch
 
+    world = dist_.world if dist_ is not None else 1
     n = 2 * GIB
     piece = 256 << 20
     h1 = torch.empty(n, dtype=torch.uint8).pin_memory()
@@ -223,25 +234,6 @@ def host_link_peaks(dev) -> dict:
     d1 = torch.empty(n, dtype=torch.uint8, device=dev)
     d2 = torch.empty(n, dtype=torch.uint8, device=dev)
     s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-
-    def timed(fn, nbytes):
-        fn()  # warm-up: first touch of the pages by the copy engines
-        torch.cuda.synchronize()
-        best = 0.0
-        for _ in range(5):
-            torch.cuda.synchronize()
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            cur = torch.cuda.current_stream()
-            a.record(cur)
-            s1.wait_stream(cur)
-            s2.wait_stream(cur)
-            fn()
-            cur.wait_stream(s1)
-            cur.wait_stream(s2)
-            b.record(cur)
-            b.synchronize()
-            best = max(best, nbytes / (a.elapsed_time(b) / 1e3) / 1e9)
-        return best
 
     def h2d():
         with torch.cuda.stream(s1):
@@ -257,9 +249,35 @@ def host_link_peaks(dev) -> dict:
         h2d()
         d2h()
 
-    out = {"h2d_gbs": timed(h2d, n), "d2h_gbs": timed(d2h, n), "bidir_gbs": timed(both, 2 * n)}
+    def timed(fn, nbytes):
+        fn()  # warm-up: first touch of the pages by the copy engines
+        torch.cuda.synchronize()
+        best = 0.0
+        for _ in range(5):
+            if dist_ is not None:
+                dist_.barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            cur = torch.cuda.current_stream()
+            a.record(cur)
+            s1.wait_stream(cur)
+            s2.wait_stream(cur)
+            fn()
+            cur.wait_stream(s1)
+            cur.wait_stream(s2)
+            b.record(cur)
+            b.synchronize()
+            t = a.elapsed_time(b) / 1e3
+            if dist_ is not None:
+                t = dist_.max(t)
+            best = max(best, nbytes * world / t / 1e9)
+        return best
+
+    box_h2d = timed(h2d, n)
+    box_d2h = timed(d2h, n)
+    box_bidir = timed(both, 2 * n)
     del h1, h2, d1, d2
-    return out
+    return {"h2d_gbs": box_h2d / world, "d2h_gbs": box_d2h / world,
+            "bidir_gbs": box_bidir / world, "box_bidir_gbs": box_bidir}
 
 
 # ---- configuration 2 state ---------------------------------------------------------
@@ -610,9 +628,8 @@ def run_kvx(args):
             per_dir = max(64, rows_fit // 2 // 16 * 16)
     except (OSError, IndexError, ValueError):
         pass
-    dist_.barrier()  # every rank measures at once: the box's concurrent peak
-    peaks = host_link_peaks(dev)
-    box_peak = dist_.sum(peaks["bidir_gbs"])
+    peaks = host_link_peaks(dev, dist_)  # all ranks at once: the box's concurrent peak
+    box_peak = peaks["box_bidir_gbs"]
     per_dir = min(per_dir, args.cache_blocks // 2)
     bench = SwapBench(dev, per_dir, args.cache_blocks)
     lists = [bench.step_lists(k) for k in range(args.warmup + args.steps)]
@@ -693,10 +710,10 @@ def run_kvx(args):
                 "unit": "GB/s",
                 "frac": value / box_peak,
                 "traffic": None,
-                "peak_source": "measured live: 2 GiB page-locked copy-engine copies (256 MiB "
-                               "pieces) H2D and D2H at once, on every GPU of the run at the "
-                               "same time (per-GPU share of the box's concurrent peak; the "
-                               "step is bidirectional)",
+                "peak_source": "measured live: every GPU of the run copies 2 GiB of "
+                               "page-locked memory each way (256 MiB pieces) in the same "
+                               "barrier-started windows; box = all bytes / slowest rank; "
+                               "per-GPU share shown (the step is bidirectional)",
                 "box_peak_gbs": box_peak,
                 "peak_h2d_gbs": peaks["h2d_gbs"],
                 "peak_d2h_gbs": peaks["d2h_gbs"],
@@ -738,7 +755,7 @@ def run_kvx(args):
         line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     dist_.finish()
     if line is not None:
-        print(json.dumps(line), flush=True)
+        emit(line)
 
 
 def bench_bytes(per_dir: int) -> int:
@@ -760,7 +777,7 @@ def run_reference(args):
 
         ref = build_ref.load_module()
     except Exception as e:  # noqa: BLE001
-        print(json.dumps({"impl": "reference", "unavailable": f"reference op not built: {e}"}))
+        emit({"impl": "reference", "unavailable": f"reference op not built: {e}"})
         return
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dev = torch.device("cuda", local)
@@ -846,7 +863,7 @@ def run_reference(args):
         "gpu_launches": 0,
         "clocks": clk,
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 # ---- configurations 1, 4 and 5 (one JSON line each, N=1 unless stated) ---------
@@ -1097,6 +1114,14 @@ def run_config5(args):
 
 
 def main():
+    # Exactly one JSON line on stdout: libraries (NCCL prints its version)
+    # write to fd 1 too, so fd 1 points at stderr while the benchmark runs and
+    # the line goes to a private copy of the original stdout.
+    out = os.fdopen(os.dup(1), "w")
+    sys.stdout.flush()
+    os.dup2(2, 1)
+    global _OUT
+    _OUT = out
     args = parse_args()
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
@@ -1105,7 +1130,7 @@ def main():
         fn = {1: run_config1, 4: run_config4, 5: run_config5}[args.config]
         line = fn(args)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            emit(line)
         return
     if args.impl == "reference":
         run_reference(args)
