@@ -58,7 +58,13 @@ def parse_args():
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["kvx", "reference"], default="kvx")
-    p.add_argument("--config", type=int, choices=[1, 2, 4, 5], default=2,
+    p.add_argument("--ref-variant", choices=["op", "live-loop"], default="op",
+                   help="reference arm, config 2: 'op' = the reference's compiled swap op "
+                        "(one cudaMemcpyAsync per block and tensor); 'live-loop' = a "
+                        "restatement of Worker.swap_blocks' hot loop (worker.py:2270-2329: "
+                        "one torch copy_ per segment and block into composite host rows), "
+                        "which cannot run as-is without Ray and vLLM")
+    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=2,
                    help="BASELINE.json configuration (2 = the headline line; 3 is the "
                         "migration object of the N>=2 line)")
     p.add_argument("--mode", default="auto", help="transfer mode: auto|sm|ce|ce_extent")
@@ -795,15 +801,39 @@ def run_reference(args):
     in_host = [torch.empty_like(h).pin_memory() for h in out_host]
     s_out, s_in = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     slots = list(range(per_dir))
+    live = args.ref_variant == "live-loop"
+    if live:
+        # composite host rows: row r holds every segment's page of one block
+        page = sh.page_bytes
+        pool_out = torch.empty((per_dir, sh.num_segments * page), dtype=torch.uint8).pin_memory()
+        pool_in = torch.empty((per_dir, sh.num_segments * page), dtype=torch.uint8).pin_memory()
+        gpu_pages = [c.view(torch.uint8).view(sh.num_blocks, page) for c in caches]
+
+    def live_loop(pool, ids, is_swap_in):
+        # worker.py:2272-2329 restated: per segment, per entry, one copy_
+        for s, pages in enumerate(gpu_pages):
+            off = s * page
+            for row, blk in enumerate(ids):
+                cpu_page = pool[row].narrow(0, off, page)
+                if is_swap_in:
+                    pages[blk].narrow(0, 0, page).copy_(cpu_page, non_blocking=True)
+                else:
+                    cpu_page.copy_(pages[blk].narrow(0, 0, page), non_blocking=True)
 
     def step(k):
         out_ids, in_ids = workloads.swap_step_ids(sh.num_blocks, per_dir, k)
         with torch.cuda.stream(s_out):
-            for c, h in zip(caches, out_host):
-                ref.swap(out_ids, slots, False, c, h)
+            if live:
+                live_loop(pool_out, out_ids, False)
+            else:
+                for c, h in zip(caches, out_host):
+                    ref.swap(out_ids, slots, False, c, h)
         with torch.cuda.stream(s_in):
-            for c, h in zip(caches, in_host):
-                ref.swap(slots, in_ids, True, c, h)
+            if live:
+                live_loop(pool_in, in_ids, True)
+            else:
+                for c, h in zip(caches, in_host):
+                    ref.swap(slots, in_ids, True, c, h)
         ev_o, ev_i = torch.cuda.Event(), torch.cuda.Event()
         ev_o.record(s_out)
         ev_i.record(s_in)
@@ -851,8 +881,11 @@ def run_reference(args):
                         f"[4096,16,32,128] fp16; per step {per_dir} random blocks out and "
                         f"{per_dir} in, out and in on two streams",
             "blocks_per_direction": per_dir,
-            "api": "reference aegaeon.ops.swap (ops/swap.cu, built unmodified from the "
-                   "reference sources): one call per K/V tensor, one cudaMemcpyAsync per block",
+            "api": ("restated Worker.swap_blocks hot loop (worker.py:2270-2329): one torch "
+                    "copy_(non_blocking=True) per segment and block into composite host rows"
+                    if live else
+                    "reference aegaeon.ops.swap (ops/swap.cu, built unmodified from the "
+                    "reference sources): one call per K/V tensor, one cudaMemcpyAsync per block"),
             "l2": "no flush needed: 8 GiB per direction per step",
         },
         "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "reference",
@@ -1113,6 +1146,71 @@ def run_config5(args):
     return line
 
 
+def run_config3_reference(args):
+    """The reference's prefill->decode route (prefill_scheduler.py:84-99,
+    decode_scheduler.py:336-347): the prefill GPU swaps the request's blocks
+    out to page-locked host memory with the reference op, then the decode GPU
+    swaps them in.  One process drives cuda:0 (prefill) and cuda:1 (decode);
+    the time is the sum of the two hops (the decode side starts after the
+    prefill side finished)."""
+    import torch
+
+    from aegaeon_b200 import workloads
+
+    if torch.cuda.device_count() < 2:
+        return {"impl": "reference", "unavailable": "config 3 needs two visible GPUs"}
+    ref = _ref_module()
+    sh = workloads.CFG3
+    plan = workloads.migration_plan(sh, requests=8, seed=0, pair=0)
+    n = plan.num_blocks
+    shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+    d0, d1 = torch.device("cuda", 0), torch.device("cuda", 1)
+    g = torch.Generator(device=d0).manual_seed(100)
+    src = [torch.empty(shape, dtype=sh.dtype, device=d0).normal_(generator=g)
+           for _ in range(sh.num_segments)]
+    dst = [torch.zeros(shape, dtype=sh.dtype, device=d1) for _ in range(sh.num_segments)]
+    host = [torch.empty((n,) + shape[1:], dtype=sh.dtype).pin_memory() for _ in src]
+    slots = list(range(n))
+
+    def hop(dev, fn):
+        with torch.cuda.device(dev):
+            s = torch.cuda.current_stream(dev)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(s)
+            fn()
+            b.record(s)
+            b.synchronize()
+            return a.elapsed_time(b) / 1e3
+
+    def out_hop():
+        for c, h in zip(src, host):
+            ref.swap(plan.source_ids, slots, False, c, h)
+
+    def in_hop():
+        for c, h in zip(dst, host):
+            ref.swap(slots, plan.target_ids, True, c, h)
+
+    for _ in range(args.warmup):
+        hop(d0, out_hop)
+        hop(d1, in_hop)
+    t = 0.0
+    for _ in range(args.steps):
+        t += hop(d0, out_hop) + hop(d1, in_hop)
+    exact = all(torch.equal(b[plan.target_ids].cpu().view(torch.uint8),
+                            a[plan.source_ids].cpu().view(torch.uint8)) for a, b in zip(src, dst))
+    nbytes = n * sh.composite_bytes
+    value = nbytes * args.steps / t / 1e9
+    return {"impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 2,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": t / args.steps * 1e3,
+            "higher_is_better": True, "dtype": "u8", "bit_exact": exact,
+            "config": {"workload": "cfg3 P->D handoff of 8 requests (prompts U{512..8192}, "
+                                   f"{n} blocks, {nbytes} B) on the reference route: "
+                                   "swap-out on the prefill GPU to host, swap-in on the decode "
+                                   "GPU, reference op (one cudaMemcpyAsync per block and tensor)"},
+            "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
 def main():
     # Exactly one JSON line on stdout: libraries (NCCL prints its version)
     # write to fd 1 too, so fd 1 points at stderr while the benchmark runs and
@@ -1126,6 +1224,14 @@ def main():
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
         if args.config in (1, 4) and rank != 0:
+            return
+        if args.config == 3:
+            if args.impl != "reference":
+                emit({"impl": "kvx", "note": "config 3 (migration) is measured by the default "
+                      "run at N >= 2 (its 'migration' object)"})
+                return
+            if rank == 0:
+                emit(run_config3_reference(args))
             return
         fn = {1: run_config1, 4: run_config4, 5: run_config5}[args.config]
         line = fn(args)
