@@ -53,6 +53,36 @@ __device__ __forceinline__ void st16(void* p, uint4 v) {
                : "memory");
 }
 
+// 32-byte accesses (sm_100 256-bit global loads / stores).
+struct V32 {
+  uint4 a, b;
+};
+
+__device__ __forceinline__ V32 ld_dev32(const void* p) {
+  V32 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r.a.x), "=r"(r.a.y), "=r"(r.a.z), "=r"(r.a.w), "=r"(r.b.x),
+                 "=r"(r.b.y), "=r"(r.b.z), "=r"(r.b.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ V32 ld_host32(const void* p) {
+  V32 r;
+  asm volatile("ld.global.cs.v8.u32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r.a.x), "=r"(r.a.y), "=r"(r.a.z), "=r"(r.a.w), "=r"(r.b.x),
+                 "=r"(r.b.y), "=r"(r.b.z), "=r"(r.b.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ void st32(void* p, const V32& v) {
+  asm volatile("st.global.cs.v8.u32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v.a.x),
+               "r"(v.a.y), "r"(v.a.z), "r"(v.a.w), "r"(v.b.x), "r"(v.b.y), "r"(v.b.z),
+               "r"(v.b.w)
+               : "memory");
+}
+
 // Largest i with items[i].tile_begin <= t (items sorted, items[0].tile_begin == 0).
 __device__ __forceinline__ uint32_t find_item(const Item* __restrict__ items,
                                               uint32_t n_items, uint32_t t) {
@@ -76,9 +106,32 @@ __device__ __forceinline__ void cta_span(uint32_t n_tiles, uint32_t* t0,
 }
 
 template <int kSrc>
+__device__ __forceinline__ void cta_copy32(const char* __restrict__ s, char* __restrict__ d,
+                                           uint32_t n) {
+  constexpr int kU = kVecUnroll / 2;  // same bytes in flight per thread as 8 x 16 B
+  const uint32_t n32 = n >> 5;
+  for (uint32_t base = threadIdx.x; base < n32; base += kVecThreads * kU) {
+    V32 r[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const uint32_t k = base + u * kVecThreads;
+      if (k < n32) r[u] = kSrc == kSrcHost ? ld_host32(s + 32ull * k) : ld_dev32(s + 32ull * k);
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const uint32_t k = base + u * kVecThreads;
+      if (k < n32) st32(d + 32ull * k, r[u]);
+    }
+  }
+}
+
+template <int kSrc, int kVec = 16>
 __device__ __forceinline__ void cta_copy(const char* __restrict__ s,
                                          char* __restrict__ d, uint32_t n) {
-  if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d) | n) &
+  if (kVec == 32 && ((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d) | n) &
+                     31u) == 0) {
+    cta_copy32<kSrc>(s, d, n);
+  } else if (((reinterpret_cast<uintptr_t>(s) | reinterpret_cast<uintptr_t>(d) | n) &
        15u) == 0) {
     const uint32_t n16 = n >> 4;
     const uint4* s16 = reinterpret_cast<const uint4*>(s);
@@ -132,7 +185,7 @@ struct GridList {
   }
 };
 
-template <int kSrc, class List>
+template <int kSrc, class List, int kVec = 16>
 __global__ void __launch_bounds__(kVecThreads)
     kvx_copy_vec(List list, uint32_t n_tiles, uint32_t tile_shift) {
   uint32_t t0, t1;
@@ -143,7 +196,7 @@ __global__ void __launch_bounds__(kVecThreads)
     uint64_t src, dst;
     uint32_t n;
     list.get(cur, t, tile_shift, &src, &dst, &n);
-    cta_copy<kSrc>(reinterpret_cast<const char*>(src), reinterpret_cast<char*>(dst), n);
+    cta_copy<kSrc, kVec>(reinterpret_cast<const char*>(src), reinterpret_cast<char*>(dst), n);
   }
 }
 

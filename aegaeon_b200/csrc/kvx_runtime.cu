@@ -73,10 +73,12 @@ int from_plan(const Error& e) {
 // ---- tunables ----------------------------------------------------------------
 struct Tunables {
   int64_t sm_ctas_host = 0;    // 0: number of SMs
-  int64_t sm_ctas_dev = 0;     // 0: 8 x number of SMs
+  int64_t sm_ctas_dev = 0;     // 0: 4 x number of SMs
   int64_t ce_min_run = 1ll << 20;
   int64_t staging_bytes = 256ll << 20;
   int64_t ce_pipeline = 0;  // double-buffered staging with a helper stream
+  int64_t vec_bytes = 32;   // bytes per thread access of the vector kernel (16 or 32)
+  int64_t bulk_ctas_per_sm = 2;  // CTAs per SM of the TMA kernel (1 or 2)
 };
 std::mutex g_tun_mu;
 Tunables g_tun;
@@ -96,6 +98,8 @@ Tunables tunables() {
     g_tun.ce_min_run = env_i64("KVX_CE_MIN_RUN", g_tun.ce_min_run);
     g_tun.staging_bytes = env_i64("KVX_STAGING_BYTES", g_tun.staging_bytes);
     g_tun.ce_pipeline = env_i64("KVX_CE_PIPELINE", g_tun.ce_pipeline);
+    g_tun.vec_bytes = env_i64("KVX_VEC_BYTES", g_tun.vec_bytes) == 16 ? 16 : 32;
+    g_tun.bulk_ctas_per_sm = env_i64("KVX_BULK_CTAS_PER_SM", g_tun.bulk_ctas_per_sm) == 1 ? 1 : 2;
   });
   std::lock_guard<std::mutex> g(g_tun_mu);
   return g_tun;
@@ -290,7 +294,7 @@ enum class Path { kHostSrc, kHostDst, kDevice, kPeer };
 int ctas_for(const DeviceState* st, Path p, const Tunables& tn) {
   if (p == Path::kHostSrc || p == Path::kHostDst)
     return int(tn.sm_ctas_host > 0 ? tn.sm_ctas_host : st->sms);
-  return int(tn.sm_ctas_dev > 0 ? tn.sm_ctas_dev : 8 * st->sms);
+  return int(tn.sm_ctas_dev > 0 ? tn.sm_ctas_dev : 4 * st->sms);
 }
 
 bool all_aligned16(const std::vector<Copy>& v) {
@@ -366,15 +370,24 @@ template <class List>
 void launch_list(const List& list, const Launch& l, const DeviceState* st, cudaStream_t s,
                  const Tunables& tn) {
   if (l.bulk) {
-    // Two 96 KiB CTAs fit on an SM.
-    const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(2 * st->sms));
+    // Up to two 96 KiB CTAs fit on an SM.
+    const uint32_t grid =
+        std::min<uint32_t>(l.n_tiles, uint32_t(tn.bulk_ctas_per_sm * st->sms));
     kvx_copy_bulk<List><<<grid, 32, kBulkSmem, s>>>(list, l.n_tiles);
   } else {
     const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(ctas_for(st, l.path, tn)));
-    if (l.path == Path::kHostSrc)
+    const bool host_src = l.path == Path::kHostSrc;
+    if (tn.vec_bytes == 32) {
+      if (host_src)
+        kvx_copy_vec<kSrcHost, List, 32><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles, kVecShift);
+      else
+        kvx_copy_vec<kSrcDevice, List, 32><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles,
+                                                                        kVecShift);
+    } else if (host_src) {
       kvx_copy_vec<kSrcHost, List><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles, kVecShift);
-    else
+    } else {
       kvx_copy_vec<kSrcDevice, List><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles, kVecShift);
+    }
   }
 }
 

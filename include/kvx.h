@@ -257,9 +257,11 @@ int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream);
  *   staging_bytes: size of each staging area of the copy-engine mode
  *                  (one per direction and device, 256 MiB by default)
  * Environment: KVX_SM_CTAS_HOST, KVX_SM_CTAS_DEV, KVX_CE_MIN_RUN,
- * KVX_STAGING_BYTES, and KVX_CE_PIPELINE=1 to double-buffer the staging area
+ * KVX_STAGING_BYTES, KVX_CE_PIPELINE=1 to double-buffer the staging area
  * (gather/scatter of one half on an internal stream while the copy engines
- * move the other; helps a single direction, hurts concurrent directions). */
+ * move the other; helps a single direction, hurts concurrent directions),
+ * KVX_VEC_BYTES (32 default: 256-bit loads/stores where aligned; 16) and
+ * KVX_BULK_CTAS_PER_SM (2 default; 1). */
 int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
                   int64_t ce_min_run, int64_t staging_bytes,
                   int64_t ce_pipeline /* -1 keep, 0 off, 1 on */);
