@@ -93,7 +93,8 @@ SIGNATURES = {
     "kvx_last_mode": (_int, []),
     "kvx_kernel_launches": (_u64, []),
     "kvx_kernel_timing": (_int, [_int]),
-    "kvx_kernel_timing_read": (_int, [_p_u64, ctypes.POINTER(ctypes.c_double), _p_u64]),
+    "kvx_kernel_timing_read": (_int, [_p_u64, ctypes.POINTER(ctypes.c_double),
+                                       ctypes.POINTER(ctypes.c_double), _p_u64]),
     "kvx_device_status": (_int, [_int, _int, ctypes.POINTER(_int)]),
     "kvx_selftest_bounded_wait": (_int, [_u64, _vp]),
     "kvx_configure": (_int, [_i64, _i64, _i64, _i64, _i64]),
@@ -202,10 +203,13 @@ def kernel_timing(enable: bool) -> None:
     check(lib().kvx_kernel_timing(1 if enable else 0))
 
 
-def kernel_timing_read() -> tuple[int, float, int]:
-    """(launches, summed kernel milliseconds, HBM bytes) since the last read."""
+def kernel_timing_read() -> tuple[int, float, float, int]:
+    """(launches, summed kernel ms, busy ms with overlaps counted once, HBM
+    bytes) since the last read."""
     n = ctypes.c_uint64()
     ms = ctypes.c_double()
+    busy = ctypes.c_double()
     b = ctypes.c_uint64()
-    check(lib().kvx_kernel_timing_read(ctypes.byref(n), ctypes.byref(ms), ctypes.byref(b)))
-    return n.value, ms.value, b.value
+    check(lib().kvx_kernel_timing_read(ctypes.byref(n), ctypes.byref(ms), ctypes.byref(busy),
+                                       ctypes.byref(b)))
+    return n.value, ms.value, busy.value, b.value

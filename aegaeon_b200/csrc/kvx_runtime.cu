@@ -898,7 +898,8 @@ int kvx_kernel_timing(int enable) {
   return KVX_OK;
 }
 
-int kvx_kernel_timing_read(uint64_t* launches, double* total_ms, uint64_t* hbm_bytes) {
+int kvx_kernel_timing_read(uint64_t* launches, double* total_ms, double* busy_ms,
+                           uint64_t* hbm_bytes) {
   t_last_error.clear();
   std::vector<TimedLaunch> v;
   {
@@ -908,19 +909,48 @@ int kvx_kernel_timing_read(uint64_t* launches, double* total_ms, uint64_t* hbm_b
   uint64_t n = 0, bytes = 0;
   double ms = 0;
   int rc = KVX_OK;
+  // Intervals relative to the first launch of each device, to merge the
+  // launches that overlapped (several streams) into busy time.
+  std::map<int, std::vector<std::pair<double, double>>> spans;
+  std::map<int, cudaEvent_t> ref;
   for (TimedLaunch& t : v) {
-    float e = 0;
+    float e = 0, b0 = 0, e0 = 0;
     cudaError_t err = cudaEventSynchronize(t.end);
     if (err == cudaSuccess) err = cudaEventElapsedTime(&e, t.begin, t.end);
+    if (!ref.count(t.device)) ref[t.device] = t.begin;
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&b0, ref[t.device], t.begin);
+    if (err == cudaSuccess) err = cudaEventElapsedTime(&e0, ref[t.device], t.end);
     if (err != cudaSuccess && rc == KVX_OK) rc = cuda_error(err, "cudaEventElapsedTime");
-    cudaEventDestroy(t.begin);
-    cudaEventDestroy(t.end);
     ++n;
     ms += e;
     bytes += t.hbm_bytes;
+    spans[t.device].emplace_back(b0, e0);
+  }
+  double busy = 0;
+  for (auto& kv : spans) {
+    auto& iv = kv.second;
+    std::sort(iv.begin(), iv.end());
+    double cb = 0, ce = 0;
+    bool open = false;
+    for (const auto& x : iv) {
+      if (!open || x.first > ce) {
+        if (open) busy += ce - cb;
+        cb = x.first;
+        ce = x.second;
+        open = true;
+      } else if (x.second > ce) {
+        ce = x.second;
+      }
+    }
+    if (open) busy += ce - cb;
+  }
+  for (TimedLaunch& t : v) {
+    cudaEventDestroy(t.begin);
+    cudaEventDestroy(t.end);
   }
   if (launches) *launches = n;
   if (total_ms) *total_ms = ms;
+  if (busy_ms) *busy_ms = busy;
   if (hbm_bytes) *hbm_bytes = bytes;
   return rc;
 }

@@ -234,10 +234,12 @@ uint64_t kvx_kernel_launches(void);
 /* Per-launch timing of the copy kernels: while enabled, every launch is
  * bracketed by two CUDA events on its stream.  _read synchronizes those
  * events and returns, since the previous read, the number of launches, their
- * summed durations and the HBM bytes they move (read + write when both sides
- * are local memory, one side when the other is host or peer memory). */
+ * summed durations, the busy time (union of the launch intervals per device:
+ * launches on different streams that overlapped count once) and the HBM bytes
+ * they move (read + write when both sides are local memory, one side when the
+ * other is host or peer memory). */
 int kvx_kernel_timing(int enable);
-int kvx_kernel_timing_read(uint64_t* launches, double* total_ms,
+int kvx_kernel_timing_read(uint64_t* launches, double* total_ms, double* busy_ms,
                            uint64_t* hbm_bytes);
 int kvx_device_status(int device, int reset, int* status_out);
 
