@@ -153,15 +153,17 @@ def check(status: int) -> None:
 
 
 def i64_array(values) -> ctypes.Array:
-    """Python ints (list/tuple/array/ndarray) -> contiguous int64 C array."""
-    try:
-        import numpy as np
+    """Block ids (list, tuple, array, numpy array or CPU/CUDA tensor) ->
+    contiguous int64 C array."""
+    import numpy as np
 
-        if isinstance(values, np.ndarray):
-            a = np.ascontiguousarray(values, dtype=np.int64)
-            return (ctypes.c_int64 * a.size).from_buffer_copy(a)
-    except ImportError:  # pragma: no cover
-        pass
+    if hasattr(values, "detach") and hasattr(values, "cpu"):  # torch tensor
+        values = values.detach().cpu().numpy()
+    if isinstance(values, np.ndarray):
+        a = np.ascontiguousarray(values.reshape(-1), dtype=np.int64)
+        if a.size == 0:
+            return (ctypes.c_int64 * 0)()
+        return (ctypes.c_int64 * a.size).from_buffer_copy(a)
     return (ctypes.c_int64 * len(values))(*values)
 
 

@@ -182,6 +182,11 @@ class KVSwapper:
                  tp_rank: int = 0, tp_size: int = 1):
         if len(segment_pages) != len(segments) or len(segment_owners) != len(segments):
             raise ValueError("segments, segment_pages and segment_owners differ in length")
+        if kv_swap is not None and kv_swap.is_cuda:
+            raise ValueError("kv_swap must be a host (CPU) tensor")
+        for t, s in zip(segment_pages, segments):
+            if not t.is_cuda:
+                raise ValueError(f"segment {s.layer_name}: pages must be a CUDA tensor")
         self.device = torch.device("cuda", device) if isinstance(device, int) else torch.device(device)
         self.device_index = self.device.index if self.device.index is not None else 0
         self.segments = list(segments)

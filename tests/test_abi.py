@@ -54,3 +54,16 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(_lib, "LIB_PATH", str(tmp_path / "nope.so"))
     with pytest.raises(RuntimeError, match="missing"):
         _lib.lib()
+
+
+def test_id_arrays_from_any_sequence():
+    import numpy as np
+    import torch
+
+    from aegaeon_b200 import _lib
+
+    for v in ([3, 1, 2], (3, 1, 2), np.array([3, 1, 2], dtype=np.int32), torch.tensor([3, 1, 2])):
+        a = _lib.i64_array(v)
+        assert list(a) == [3, 1, 2]
+    assert len(_lib.i64_array([])) == 0
+    assert len(_lib.i64_array(np.zeros(0, dtype=np.int64))) == 0
