@@ -75,10 +75,11 @@ struct Tunables {
   int64_t sm_ctas_host = 0;    // 0: number of SMs
   int64_t sm_ctas_dev = 0;     // 0: 4 x number of SMs
   int64_t ce_min_run = 1ll << 20;
-  int64_t staging_bytes = 256ll << 20;
+  int64_t staging_bytes = 1ll << 30;
   int64_t ce_pipeline = 0;  // double-buffered staging with a helper stream
   int64_t vec_bytes = 32;   // bytes per thread access of the vector kernel (16 or 32)
   int64_t bulk_ctas_per_sm = 2;  // CTAs per SM of the TMA kernel (1 or 2)
+  int64_t staging_bulk = 1;      // staging gather/scatter: 1 TMA kernel, 0 vector kernel
 };
 std::mutex g_tun_mu;
 Tunables g_tun;
@@ -100,6 +101,7 @@ Tunables tunables() {
     g_tun.ce_pipeline = env_i64("KVX_CE_PIPELINE", g_tun.ce_pipeline);
     g_tun.vec_bytes = env_i64("KVX_VEC_BYTES", g_tun.vec_bytes) == 16 ? 16 : 32;
     g_tun.bulk_ctas_per_sm = env_i64("KVX_BULK_CTAS_PER_SM", g_tun.bulk_ctas_per_sm) == 1 ? 1 : 2;
+    g_tun.staging_bulk = env_i64("KVX_STAGING_BULK", g_tun.staging_bulk) ? 1 : 0;
   });
   std::lock_guard<std::mutex> g(g_tun_mu);
   return g_tun;
@@ -654,7 +656,8 @@ int run_ce_grid(DeviceState* st, const GridPlan& p, cudaStream_t s, const Tunabl
       else
         rr.push_back(Run{h, st_off, span});
     }
-    rc = add_grid(&up, &launches, &chunk, Path::kDevice, grid_aligned16(chunk));
+    rc = add_grid(&up, &launches, &chunk, Path::kDevice,
+                  tn.staging_bulk && grid_aligned16(chunk));
     if (rc) return rc;
     runs.push_back(std::move(rr));
     buf_of.push_back(b);
@@ -798,7 +801,7 @@ int execute_host_copies(DeviceState* st, std::vector<Copy>& copies, bool is_swap
     for (Copy& c : copies) (is_swap_in ? c.src : c.dst) += delta;
     rc = run_sm(st, copies, waves, is_swap_in ? Path::kHostSrc : Path::kHostDst, false, s, tn);
   } else if (mode == KVX_MODE_CE) {
-    rc = run_ce_staged(st, copies, waves, is_swap_in, true, s, tn);
+    rc = run_ce_staged(st, copies, waves, is_swap_in, tn.staging_bulk != 0, s, tn);
   } else if (mode == KVX_MODE_CE_EXTENT) {
     rc = run_ce_extent(copies, waves, s);
   } else {
@@ -840,7 +843,7 @@ int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
       rc = run_ce_grid(st, *p, s, tn);
     } else {
       const std::vector<Copy> v = grid_copies(*p);
-      rc = run_ce_staged(st, v, {v.size()}, is_swap_in, true, s, tn);
+      rc = run_ce_staged(st, v, {v.size()}, is_swap_in, tn.staging_bulk != 0, s, tn);
     }
   } else if (mode == KVX_MODE_CE_EXTENT) {
     const std::vector<Copy> v = grid_copies(*p);

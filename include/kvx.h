@@ -257,7 +257,7 @@ int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream);
  *   sm_ctas_dev  : CTAs of an SM kernel that touches device memory only
  *   ce_min_run   : mean coalesced host-run bytes from which AUTO uses the CE
  *   staging_bytes: size of each staging area of the copy-engine mode
- *                  (one per direction and device, 256 MiB by default)
+ *                  (one per direction and device, 1 GiB by default)
  * Environment: KVX_SM_CTAS_HOST, KVX_SM_CTAS_DEV, KVX_CE_MIN_RUN,
  * KVX_STAGING_BYTES, KVX_CE_PIPELINE=1 to double-buffer the staging area
  * (gather/scatter of one half on an internal stream while the copy engines

@@ -235,7 +235,7 @@ def test_staged_chunks_parity(cuda, oracle, pipeline):
                 assert np.array_equal(t.cpu().numpy(), e)
             host_ids = torch.randperm(rows, generator=g)[:70].tolist()
     finally:
-        _lib.configure(staging_bytes=256 << 20, ce_pipeline=0)
+        _lib.configure(staging_bytes=1 << 30, ce_pipeline=0)
         sw.close()
 
 
