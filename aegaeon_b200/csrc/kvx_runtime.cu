@@ -820,13 +820,22 @@ int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
     t_last_mode = mode == KVX_MODE_AUTO ? KVX_MODE_SM : mode;
     return KVX_OK;
   }
+  // Partial extents leave gaps in the host rows: their host runs come from the
+  // expanded copy list (computed once, reused by the copy-engine path).
+  std::vector<Copy> expanded;
+  const bool partial = p->row_span == 0;
   if (mode == KVX_MODE_AUTO) {
-    if (!hi.mapped)
+    if (!hi.mapped) {
       mode = KVX_MODE_CE;
-    else
-      mode = (tn.ce_min_run > 0 && p->row_span && grid_mean_run(*p) >= uint64_t(tn.ce_min_run))
-                 ? KVX_MODE_CE
-                 : KVX_MODE_SM;
+    } else if (tn.ce_min_run <= 0) {
+      mode = KVX_MODE_SM;
+    } else if (!partial) {
+      mode = grid_mean_run(*p) >= uint64_t(tn.ce_min_run) ? KVX_MODE_CE : KVX_MODE_SM;
+    } else {
+      expanded = grid_copies(*p);
+      mode = mean_host_run(expanded, is_swap_in) >= uint64_t(tn.ce_min_run) ? KVX_MODE_CE
+                                                                           : KVX_MODE_SM;
+    }
   }
   if (mode == KVX_MODE_SM_BULK) mode = KVX_MODE_SM;  // bulk is device-only
   int rc;
@@ -842,8 +851,9 @@ int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
     if (p->row_span && p->row_span <= staging_cap(tn)) {
       rc = run_ce_grid(st, *p, s, tn);
     } else {
-      const std::vector<Copy> v = grid_copies(*p);
-      rc = run_ce_staged(st, v, {v.size()}, is_swap_in, tn.staging_bulk != 0, s, tn);
+      if (expanded.empty()) expanded = grid_copies(*p);
+      rc = run_ce_staged(st, expanded, {expanded.size()}, is_swap_in, tn.staging_bulk != 0, s,
+                         tn);
     }
   } else if (mode == KVX_MODE_CE_EXTENT) {
     const std::vector<Copy> v = grid_copies(*p);

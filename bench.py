@@ -64,7 +64,7 @@ def parse_args():
                         "restatement of Worker.swap_blocks' hot loop (worker.py:2270-2329: "
                         "one torch copy_ per segment and block into composite host rows), "
                         "which cannot run as-is without Ray and vLLM")
-    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=2,
+    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6], default=2,
                    help="BASELINE.json configuration (2 = the headline line; 3 is the "
                         "migration object of the N>=2 line)")
     p.add_argument("--mode", default="auto", help="transfer mode: auto|sm|ce|ce_extent")
@@ -1216,6 +1216,107 @@ def run_config3_reference(args):
                     "d2h_bytes_per_step": 0}}
 
 
+def run_config6(args):
+    """The reference's own swap micro-benchmark workload
+    (benchmark/benchmark_composite_swap.py:117-187): 8 segments of one
+    17,301,504-byte physical page, 528-token physical blocks of 16-token
+    kernel blocks, 3 fixed (full) pages plus the attention pages of a sequence
+    of each length in [1, 128, 256, 512, 528, 529, 1057]; "full" copies every
+    page whole, "optimized" only the live prefix of the last attention page.
+    p50 / p95 of the swap time over `--steps` samples (CUDA events), H2D and
+    D2H, for this build (kvx_swap_blocks, one call) or, with --impl
+    reference, the harness's own copy loop restated (one torch copy_ per
+    segment and page, benchmark_composite_swap.py:67-87)."""
+    import math
+
+    import torch
+
+    from aegaeon_b200 import cache_transfer as ct
+    from aegaeon_b200 import swapper
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    segments_n, fixed, phys_bytes, pbs, kbs = 8, 3, 17_301_504, 528, 16
+    seg_page = phys_bytes // segments_n
+    ratio = pbs // kbs
+    results = {}
+    for length in (1, 128, 256, 512, 528, 529, 1057):
+        attn = math.ceil(length / pbs)
+        total = fixed + attn
+        extents = {"full": [(0, ratio)] * total, "optimized": [(0, ratio)] * fixed}
+        for b in range(attn):
+            extents["optimized"].append(
+                ct.kernel_block_extent_for_attention_page(length, b, pbs, kbs, None))
+        cpu_pages = torch.empty((total, phys_bytes), dtype=torch.uint8).pin_memory()
+        gpu = [torch.empty((total, seg_page), dtype=torch.uint8, device=dev)
+               for _ in range(segments_n)]
+        segs = [swapper.CacheSegment(f"s{i}", (f"s{i}",), i * seg_page, seg_page)
+                for i in range(segments_n)]
+        sw = None
+        if args.impl != "reference":
+            sw = swapper.KVSwapper(0, segs, [g.view(-1) for g in gpu], [frozenset({0})] * segments_n,
+                                   [ratio], kv_swap=cpu_pages.view(-1))
+        stream = torch.cuda.Stream(dev)
+        row = {}
+        for kind, ext in extents.items():
+            ids = list(range(total))
+            first = [f for f, _ in ext]
+            valid = [v for _, v in ext]
+            for direction, is_in in (("H2D", True), ("D2H", False)):
+                def submit():
+                    if sw is not None:
+                        sw.swap_blocks([0], ids, ids, [0] * total, first, valid, [None], is_in,
+                                       stream=stream)
+                        return
+                    with torch.cuda.stream(stream):
+                        for si, gp in enumerate(gpu):
+                            for page, (f, v) in enumerate(ext):
+                                off, ln = ct.byte_extent_for_kernel_blocks(seg_page, ratio, f, v)
+                                if ln == 0:
+                                    continue
+                                c = cpu_pages[page].narrow(0, si * seg_page + off, ln)
+                                g = gp[page].narrow(0, off, ln)
+                                if is_in:
+                                    g.copy_(c, non_blocking=True)
+                                else:
+                                    c.copy_(g, non_blocking=True)
+
+                for _ in range(args.warmup):
+                    submit()
+                stream.synchronize()
+                samples = []
+                for _ in range(args.steps):
+                    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    a.record(stream)
+                    submit()
+                    b.record(stream)
+                    b.synchronize()
+                    samples.append(a.elapsed_time(b))
+                samples.sort()
+                nbytes = sum(ct.byte_extent_for_kernel_blocks(seg_page, ratio, f, v)[1]
+                             for f, v in ext) * segments_n
+                row[f"{kind}_{direction}"] = {
+                    "p50_ms": samples[len(samples) // 2],
+                    "p95_ms": samples[math.ceil(0.95 * len(samples)) - 1],
+                    "bytes": nbytes,
+                    "gbs_at_p50": nbytes / (samples[len(samples) // 2] / 1e3) / 1e9}
+        results[str(length)] = row
+        if sw is not None:
+            sw.close()
+        del gpu, cpu_pages
+        torch.cuda.empty_cache()
+    head = results["1057"]["optimized_H2D"]
+    return {"impl": args.impl, "metric": METRIC, "value": head["gbs_at_p50"], "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "u8",
+            "config": {"workload": "benchmark_composite_swap.py defaults: 8 segments, 3 fixed "
+                                   "pages, 17,301,504-byte physical page, 528-token physical / "
+                                   "16-token kernel blocks; value = optimized H2D at length 1057",
+                       "api": "kvx_swap_blocks (one call per swap)" if args.impl != "reference"
+                       else "restated harness loop: one torch copy_ per segment and page"},
+            "per_length": results}
+
+
 def main():
     # Exactly one JSON line on stdout: libraries (NCCL prints its version)
     # write to fd 1 too, so fd 1 points at stderr while the benchmark runs and
@@ -1237,6 +1338,10 @@ def main():
                 return
             if rank == 0:
                 emit(run_config3_reference(args))
+            return
+        if args.config == 6:
+            if rank == 0:
+                emit(run_config6(args))
             return
         fn = {1: run_config1, 4: run_config4, 5: run_config5}[args.config]
         line = fn(args)
