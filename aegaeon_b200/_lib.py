@@ -159,12 +159,13 @@ def i64_array(values) -> ctypes.Array:
 
     if hasattr(values, "detach") and hasattr(values, "cpu"):  # torch tensor
         values = values.detach().cpu().numpy()
-    if isinstance(values, np.ndarray):
-        a = np.ascontiguousarray(values.reshape(-1), dtype=np.int64)
-        if a.size == 0:
-            return (ctypes.c_int64 * 0)()
-        return (ctypes.c_int64 * a.size).from_buffer_copy(a)
-    return (ctypes.c_int64 * len(values))(*values)
+    # One conversion into a fresh int64 array, then a zero-copy ctypes view
+    # (the view keeps the array alive); much faster than building the ctypes
+    # array element by element for long id lists.
+    a = np.array(values, dtype=np.int64).reshape(-1)
+    if a.size == 0:
+        return (ctypes.c_int64 * 0)()
+    return (ctypes.c_int64 * a.size).from_buffer(a)
 
 
 def mode_of(mode) -> int:
