@@ -469,13 +469,27 @@ def cpu_baseline(seconds: float) -> dict:
         if time.perf_counter() - t0 >= seconds:
             break
     dt = time.perf_counter() - t0
+    # The same gather with torch.index_select over a block-shaped host tensor,
+    # on all host threads (the CPU path named by the configuration).
+    import torch
+
+    torch.set_num_threads(threads)
+    src_t = torch.from_numpy(src).view(nsrc, page)
+    idx = torch.tensor(ids, dtype=torch.int64)
+    out_t = torch.index_select(src_t, 0, idx)
+    t1 = time.perf_counter()
+    reps_t = 0
+    while time.perf_counter() - t1 < min(seconds, 5.0):
+        torch.index_select(src_t, 0, idx, out=out_t)
+        reps_t += 1
+    torch_gbs = reps_t * ngather * page / (time.perf_counter() - t1) / 1e9
     cpu = "unknown"
     try:
         cpu = [l for l in open("/proc/cpuinfo") if l.startswith("model name")][0].split(":")[1].strip()
     except (OSError, IndexError):
         pass
     return {"value": reps * ngather * page / dt / 1e9, "unit": "GB/s", "cores": threads,
-            "kind": "port",
+            "kind": "port", "torch_index_select_gbs": torch_gbs,
             "sample": f"{reps} x gather of {ngather} random 128 KiB blocks (512 MiB) from a "
                       f"2 GiB host cache, {threads} threads, {dt:.1f} s; cpu {cpu}"}
 

@@ -69,3 +69,20 @@ def test_native_events_local(cuda):
     again = kev.Event(interprocess=True)
     assert again.handle == handle  # reused from the pool
     again.release()
+
+
+def test_chunked_upload_parity(cuda):
+    """kvx_upload_chunked (the weight upload of a model switch) moves the
+    exact bytes, with chunk sizes that do not divide the length."""
+    from aegaeon_b200 import _lib
+
+    n = (3 << 20) + 12345
+    host = torch.randint(0, 255, (n,), dtype=torch.uint8).pin_memory()
+    dev = torch.zeros(n, dtype=torch.uint8, device=cuda)
+    s = torch.cuda.current_stream()
+    for chunk in (1 << 20, 4096 + 7, n, 0):
+        dev.zero_()
+        _lib.check(_lib.lib().kvx_upload_chunked(dev.data_ptr(), host.data_ptr(), n, chunk,
+                                                 s.cuda_stream))
+        torch.cuda.synchronize()
+        assert torch.equal(dev.cpu(), host)
