@@ -7,6 +7,7 @@ entry point raises ``RuntimeError`` naming the build command.
 
 from __future__ import annotations
 
+import array
 import ctypes
 import os
 import threading
@@ -136,6 +137,38 @@ def lib() -> ctypes.CDLL:
     return _lib
 
 
+_shim = None
+
+
+def shim():
+    """The compiled call shim (``aegaeon_b200/_kvxcall*.so``, built with the
+    library) bound to the functions of ``lib()``; raises if it is missing."""
+    global _shim
+    if _shim is not None:
+        return _shim
+    handle = lib()
+    with _lock:
+        if _shim is None:
+            try:
+                from . import _kvxcall
+            except ImportError as e:
+                raise RuntimeError(
+                    f"the kvx call shim is missing ({e}); build it with "
+                    "`python -c 'import __graft_entry__ as g; g.build()'` "
+                    "or `python -m aegaeon_b200.build`"
+                ) from e
+            _kvxcall.bind(ctypes.cast(handle.kvx_swap, ctypes.c_void_p).value,
+                          ctypes.cast(handle.kvx_swap_blocks, ctypes.c_void_p).value)
+            _shim = _kvxcall
+    return _shim
+
+
+def ids_arg(values):
+    """Block ids as the call shim takes them: lists and tuples as they are,
+    anything else (numpy arrays, tensors, ranges) as an int64 C array."""
+    return values if isinstance(values, (list, tuple)) else i64_array(values)
+
+
 def check(status: int) -> None:
     """Map a kvx status to the exception type the reference raises."""
     if status == KVX_OK:
@@ -153,8 +186,14 @@ def check(status: int) -> None:
 
 
 def i64_array(values) -> ctypes.Array:
-    """Block ids (list, tuple, array, numpy array or CPU/CUDA tensor) ->
-    contiguous int64 C array."""
+    """Block ids (list, tuple, range, array, numpy array or CPU/CUDA tensor)
+    -> contiguous int64 C array.  Non-integer ids raise TypeError, ids outside
+    int64 OverflowError."""
+    if isinstance(values, (list, tuple, range)):
+        # One C-level pass that rejects ids outside int64; the ctypes view
+        # keeps the array alive.
+        a = array.array("q", values)
+        return (ctypes.c_int64 * len(a)).from_buffer(a) if len(a) else (ctypes.c_int64 * 0)()
     import numpy as np
 
     if hasattr(values, "detach") and hasattr(values, "cpu"):  # torch tensor
@@ -166,6 +205,17 @@ def i64_array(values) -> ctypes.Array:
     if a.size == 0:
         return (ctypes.c_int64 * 0)()
     return (ctypes.c_int64 * a.size).from_buffer(a)
+
+
+def current_stream_handle(device_index: int) -> int:
+    """cudaStream_t of the current torch stream of a device (torch's own raw
+    accessor where it exists: several microseconds cheaper per call)."""
+    import torch
+
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return raw(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream
 
 
 def mode_of(mode) -> int:

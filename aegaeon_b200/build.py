@@ -11,6 +11,7 @@ import os
 import shutil
 import subprocess
 import sys
+import sysconfig
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
@@ -28,6 +29,8 @@ HEADERS = [
     os.path.join(ROOT, "include", "kvx.h"),
 ]
 OUT = os.path.join(HERE, "libkvx.so")
+SHIM_SOURCE = os.path.join(HERE, "csrc", "kvx_pycall.c")
+SHIM_OUT = os.path.join(HERE, "_kvxcall" + sysconfig.get_config_var("EXT_SUFFIX"))
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -45,7 +48,25 @@ def up_to_date() -> bool:
     return all(os.path.getmtime(p) <= t for p in SOURCES + HEADERS)
 
 
+def build_shim(force: bool = False) -> str:
+    """The Python call shim (plain C against the CPython headers; it reaches
+    libkvx.so through function pointers handed over at import)."""
+    deps = [SHIM_SOURCE, os.path.join(ROOT, "include", "kvx.h")]
+    if (not force and os.path.exists(SHIM_OUT)
+            and all(os.path.getmtime(p) <= os.path.getmtime(SHIM_OUT) for p in deps)):
+        return SHIM_OUT
+    cc = os.environ.get("CC") or shutil.which("gcc") or "cc"
+    cmd = [cc, "-O2", "-Wall", "-shared", "-fPIC", "-I" + sysconfig.get_paths()["include"],
+           SHIM_SOURCE, "-o", SHIM_OUT + ".tmp"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"{cc} failed ({res.returncode}):\n{res.stderr}\n{res.stdout}")
+    os.replace(SHIM_OUT + ".tmp", SHIM_OUT)
+    return SHIM_OUT
+
+
 def build(force: bool = False, verbose: bool = False) -> str:
+    build_shim(force)
     if not force and up_to_date():
         return OUT
     cmd = [

@@ -10,6 +10,8 @@
 //                    thread (32 KiB per 256-thread CTA).  Works on any memory
 //                    the SM can address: local HBM, device-mapped page-locked
 //                    host memory (PCIe) and IPC-mapped peer HBM (NVLink).
+//                    kvx_copy_vec_inline is the same kernel with a small grid
+//                    list passed by value in its parameters.
 //  * kvx_copy_bulk : local HBM only.  One elected thread runs a ring of TMA
 //                    bulk copies (cp.async.bulk global->shared completing on
 //                    an mbarrier, then shared->global in bulk groups).  Every
@@ -185,9 +187,36 @@ struct GridList {
   }
 };
 
-template <int kSrc, class List, int kVec = 16>
-__global__ void __launch_bounds__(kVecThreads)
-    kvx_copy_vec(List list, uint32_t n_tiles, uint32_t tile_shift) {
+// A grid list carried in the kernel's parameter space instead of a device
+// table: small requests launch without a descriptor upload.  Entries occupy
+// records [0, n), the segment table records [n, n + n_segs); both are 32-byte
+// records.  Sized so the whole parameter block stays within 4 KiB.
+constexpr uint32_t kInlineRecords = 124;
+
+struct InlineGridList {
+  uint32_t n = 0;       // entries
+  uint32_t n_segs = 0;  // segments
+  uint32_t pad[2] = {};
+  uint4 rec[2 * kInlineRecords];
+  __host__ __device__ __forceinline__ const GridEntry* entries() const {
+    return reinterpret_cast<const GridEntry*>(rec);
+  }
+  __host__ __device__ __forceinline__ const GridSeg* segs() const {
+    return reinterpret_cast<const GridSeg*>(rec + 2 * n);
+  }
+  __device__ __forceinline__ uint32_t seek(uint32_t t) const { return grid_find(entries(), n, t); }
+  __device__ __forceinline__ void get(uint32_t& cur, uint32_t t, uint32_t shift, uint64_t* src,
+                                      uint64_t* dst, uint32_t* len) const {
+    const GridEntry* e = entries();
+    while (cur + 1 < n && e[cur + 1].tile_begin <= t) ++cur;
+    grid_resolve(e[cur], segs(), t, shift, src, dst, len);
+  }
+};
+static_assert(sizeof(InlineGridList) + 8 <= 4096, "inline list exceeds the parameter limit");
+
+template <int kSrc, int kVec, class List>
+__device__ __forceinline__ void copy_tiles(const List& list, uint32_t n_tiles,
+                                           uint32_t tile_shift) {
   uint32_t t0, t1;
   cta_span(n_tiles, &t0, &t1);
   if (t0 >= t1) return;
@@ -198,6 +227,21 @@ __global__ void __launch_bounds__(kVecThreads)
     list.get(cur, t, tile_shift, &src, &dst, &n);
     cta_copy<kSrc, kVec>(reinterpret_cast<const char*>(src), reinterpret_cast<char*>(dst), n);
   }
+}
+
+template <int kSrc, class List, int kVec = 16>
+__global__ void __launch_bounds__(kVecThreads)
+    kvx_copy_vec(List list, uint32_t n_tiles, uint32_t tile_shift) {
+  copy_tiles<kSrc, kVec>(list, n_tiles, tile_shift);
+}
+
+// Same copy with the work list read in place from the parameter space
+// (__grid_constant__: no per-thread copy of the 4 KiB list).
+template <int kSrc, int kVec>
+__global__ void __launch_bounds__(kVecThreads)
+    kvx_copy_vec_inline(const __grid_constant__ InlineGridList list, uint32_t n_tiles,
+                        uint32_t tile_shift) {
+  copy_tiles<kSrc, kVec>(list, n_tiles, tile_shift);
 }
 
 // ---- TMA bulk copy (local HBM only) ----------------------------------------

@@ -465,6 +465,20 @@ bool unique_ids(std::vector<int64_t> ids) {
   return std::adjacent_find(ids.begin(), ids.end()) == ids.end();
 }
 
+// True when no two non-empty ranges of `a` intersect.
+bool pairwise_disjoint(std::vector<Range> a) {
+  std::sort(a.begin(), a.end(), [](const Range& x, const Range& y) { return x.b < y.b; });
+  uint64_t end = 0;
+  bool any = false;
+  for (const Range& r : a) {
+    if (r.b >= r.e) continue;
+    if (any && r.b < end) return false;
+    end = any ? std::max(end, r.e) : r.e;
+    any = true;
+  }
+  return true;
+}
+
 // Entry-level checks shared by the segmented grid builders: uniform page,
 // owners, groups, extents.  Fills out->entries (ids raw, extents set) and
 // returns false when the grid form does not apply.
@@ -524,6 +538,22 @@ std::vector<int64_t> dst_ids(const std::vector<GridEntry>& v) {
   return d;
 }
 
+// True when no block id is both a source and a target of the entries.
+bool sources_not_targets(const std::vector<GridEntry>& v) {
+  std::vector<int64_t> src;
+  src.reserve(v.size());
+  for (const GridEntry& g : v) src.push_back(g.src_id);
+  std::vector<int64_t> dst = dst_ids(v);
+  std::sort(src.begin(), src.end());
+  std::sort(dst.begin(), dst.end());
+  size_t i = 0, j = 0;
+  while (i < src.size() && j < dst.size()) {
+    if (src[i] == dst[j]) return false;
+    if (src[i] < dst[j]) ++i; else ++j;
+  }
+  return true;
+}
+
 }  // namespace
 
 bool grid_swap_blocks(const Layout& L, const Entries& e, bool is_swap_in, uint64_t host_base,
@@ -578,7 +608,15 @@ bool grid_migrate(const Layout& S, const Layout& T, const Entries& e, GridPlan* 
   if (!ids_in(out->entries, true, min_blocks(S))) return false;
   if (!ids_in(out->entries, false, min_blocks(T))) return false;
   if (!unique_ids(dst_ids(out->entries))) return false;
-  if (!disjoint_sets(page_ranges(S), page_ranges(T))) return false;
+  if (!disjoint_sets(page_ranges(S), page_ranges(T))) {
+    // Both sides are the same cache (block copies inside one GPU's cache):
+    // still one grid when its segments do not alias each other and no block
+    // is both read and written, so that no copy reads bytes another writes
+    // and any order of the copies gives the sequential result.
+    if (S.seg_pages != T.seg_pages || S.seg_num_blocks != T.seg_num_blocks ||
+        !pairwise_disjoint(page_ranges(S)) || !sources_not_targets(out->entries))
+      return false;
+  }
   out->segs.clear();
   for (size_t s = 0; s < ns; ++s)
     out->segs.push_back(GridSeg{S.seg_pages[s], page, T.seg_pages[s], page});

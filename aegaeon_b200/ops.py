@@ -57,37 +57,38 @@ def swap(
     Drop-in for ``aegaeon.ops.swap`` (ops/swap.cu:25-60).  ``mode`` selects
     the transfer engine: "auto" (default), "sm", "ce" or "ce_extent".
     """
-    n = len(source_block_ids)
-    if len(target_block_ids) != n:
-        raise ValueError(
-            f"source_block_ids has {n} ids but target_block_ids has "
-            f"{len(target_block_ids)}"
-        )
     if not kv_cache.is_cuda:
         raise ValueError("kv_cache must be a CUDA tensor")
     if kv_swap.is_cuda:
         raise ValueError("kv_swap must be a host (CPU) tensor")
-    block_bytes = reference_block_bytes(kv_cache)
-    src = _lib.i64_array(source_block_ids)
-    dst = _lib.i64_array(target_block_ids)
-    lib = _lib.lib()
-    with torch.cuda.device(kv_cache.device):
-        stream = torch.cuda.current_stream(kv_cache.device).cuda_stream
-        _lib.check(
-            lib.kvx_swap(
-                src,
-                dst,
-                n,
-                1 if is_swap_in else 0,
-                kv_cache.data_ptr(),
-                span_bytes(kv_cache),
-                block_bytes,
-                kv_swap.data_ptr(),
-                span_bytes(kv_swap),
-                _lib.mode_of(mode),
-                stream,
-            )
-        )
+    device = kv_cache.device.index
+    if torch.cuda.current_device() == device:
+        _swap_here(source_block_ids, target_block_ids, is_swap_in, kv_cache, kv_swap, mode,
+                   device)
+    else:
+        with torch.cuda.device(device):
+            _swap_here(source_block_ids, target_block_ids, is_swap_in, kv_cache, kv_swap,
+                       mode, device)
+
+
+def _swap_here(source_block_ids, target_block_ids, is_swap_in, kv_cache, kv_swap, mode,
+               device) -> None:
+    """Body of swap; runs with ``device`` (kv_cache's) current.  The call shim
+    converts the ids and checks their lengths (ValueError) in C."""
+    status = _lib.shim().swap(
+        _lib.ids_arg(source_block_ids),
+        _lib.ids_arg(target_block_ids),
+        is_swap_in,
+        kv_cache.data_ptr(),
+        span_bytes(kv_cache),
+        reference_block_bytes(kv_cache),
+        kv_swap.data_ptr(),
+        span_bytes(kv_swap),
+        _lib.mode_of(mode),
+        _lib.current_stream_handle(device),
+    )
+    if status:
+        _lib.check(status)
 
 
 def plan_swap(

@@ -137,6 +137,17 @@ class _Layout:
             pass
 
 
+def _check_lengths(source_block_ids, target_block_ids, group_ids, first_kernel_blocks,
+                   valid_kernel_blocks) -> int:
+    n = len(source_block_ids)
+    if (len(target_block_ids) == n and len(group_ids) == n and len(first_kernel_blocks) == n
+            and len(valid_kernel_blocks) == n):
+        return n
+    _entry_arrays(source_block_ids, target_block_ids, group_ids, first_kernel_blocks,
+                  valid_kernel_blocks)  # raises with the reference's message
+    raise AssertionError("unreachable")
+
+
 def _entry_arrays(source_block_ids, target_block_ids, group_ids, first_kernel_blocks,
                   valid_kernel_blocks):
     lengths = {
@@ -256,43 +267,47 @@ class KVSwapper:
         """
         if self.kv_swap_view is None:
             raise ValueError("this KVSwapper has no host pool")
-        n, src, dst, grp, first, valid = _entry_arrays(
-            source_block_ids, target_block_ids, group_ids, first_kernel_blocks,
-            valid_kernel_blocks)
+        _check_lengths(source_block_ids, target_block_ids, group_ids, first_kernel_blocks,
+                       valid_kernel_blocks)
         if stream is None:
             stream = self.swap_in_stream if is_swap_in else self.swap_out_stream
-        with torch.cuda.device(self.device):
-            if return_handle:
-                from . import events as kev
+        a = _lib.ids_arg
+        args = (request_ids, a(source_block_ids), a(target_block_ids), a(group_ids),
+                a(first_kernel_blocks), a(valid_kernel_blocks), source_events, is_swap_in, mode,
+                stream, interprocess, return_handle)
+        if torch.cuda.current_device() == self.device_index:
+            return self._swap_blocks_here(*args)
+        with torch.cuda.device(self.device_index):
+            return self._swap_blocks_here(*args)
 
-                new_event = kev.Event(interprocess=True)
-            else:
-                new_event = torch.cuda.Event(interprocess=interprocess)
-            self._wait_source_events(stream, new_event, request_ids, source_events)
-        copied = ctypes.c_uint64(0)
-        extents = ctypes.c_uint64(0)
-        with torch.cuda.device(self.device):
-            _lib.check(
-                _lib.lib().kvx_swap_blocks(
-                    self._layout.handle, n, src, dst, grp, first, valid,
-                    1 if is_swap_in else 0, _lib.mode_of(mode), stream.cuda_stream,
-                    ctypes.byref(copied), ctypes.byref(extents),
-                )
-            )
-            new_event.record(stream)
-        self.last_stats = (copied.value, extents.value)
-        full = n * self.composite_page
-        logger.debug(
-            "swap requests %s (%s to %s): copied %d/%d bytes (saved %.2f%%), %d DMA extents",
-            list(request_ids), "CPU" if is_swap_in else "GPU", "GPU" if is_swap_in else "CPU",
-            copied.value, full, 0.0 if full == 0 else 100.0 * (1 - copied.value / full),
-            extents.value,
-        )
+    def _swap_blocks_here(self, request_ids, src, dst, grp, first, valid, source_events,
+                          is_swap_in, mode, stream, interprocess, return_handle):
+        """Body of swap_blocks; runs with this cache's device current.  The call
+        shim converts the ids and checks the five lengths (ValueError) in C."""
         if return_handle:
             from . import events as kev
 
-            with torch.cuda.device(self.device):
-                return kev.reduce_event(new_event)
+            new_event = kev.Event(interprocess=True)
+        else:
+            new_event = torch.cuda.Event(interprocess=interprocess)
+        self._wait_source_events(stream, new_event, request_ids, source_events)
+        status, copied, extents = _lib.shim().swap_blocks(
+            self._layout.handle, src, dst, grp, first, valid, is_swap_in, _lib.mode_of(mode),
+            stream.cuda_stream)
+        if status:
+            _lib.check(status)
+        new_event.record(stream)
+        self.last_stats = (copied, extents)
+        if logger.isEnabledFor(logging.DEBUG):
+            full = len(src) * self.composite_page
+            logger.debug(
+                "swap requests %s (%s to %s): copied %d/%d bytes (saved %.2f%%), "
+                "%d DMA extents", list(request_ids), "CPU" if is_swap_in else "GPU",
+                "GPU" if is_swap_in else "CPU", copied, full,
+                0.0 if full == 0 else 100.0 * (1 - copied / full), extents,
+            )
+        if return_handle:
+            return kev.reduce_event(new_event)
         return new_event
 
     def plan_swap_blocks(self, source_block_ids, target_block_ids, group_ids,

@@ -64,9 +64,9 @@ def parse_args():
                         "restatement of Worker.swap_blocks' hot loop (worker.py:2270-2329: "
                         "one torch copy_ per segment and block into composite host rows), "
                         "which cannot run as-is without Ray and vLLM")
-    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6], default=2,
+    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7], default=2,
                    help="BASELINE.json configuration (2 = the headline line; 3 is the "
-                        "migration object of the N>=2 line)")
+                        "migration object of the N>=2 line; 7 = latency of small swap calls)")
     p.add_argument("--mode", default="auto", help="transfer mode: auto|sm|ce|ce_extent")
     p.add_argument("--blocks", type=int, default=1024, help="blocks per direction per step")
     p.add_argument("--cache-blocks", type=int, default=4096,
@@ -1331,6 +1331,85 @@ def run_config6(args):
             "per_length": results}
 
 
+SMALL_CALL_BLOCKS = (1, 2, 4, 16, 64, 256)
+
+
+def run_config7(args):
+    """Small swap calls, as a decode turn issues them: latency of one
+    ``swap`` call (the reference op's interface) moving n scattered blocks of
+    one cfg2 K tensor ([4096,16,32,128] fp16, 128 KiB blocks) to host slots,
+    and one moving them back in to other blocks, for n in SMALL_CALL_BLOCKS.
+    Per n: warm-up calls, then steps x 20 calls per direction timed with CUDA
+    events on the current stream and with the host clock (these calls are
+    bound by host-side issue cost, so the two agree).  Afterwards the moved
+    blocks are compared byte for byte."""
+    import torch
+
+    from aegaeon_b200 import _lib, ops, workloads
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    sh = workloads.CFG2
+    shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    cache = torch.empty(shape, dtype=sh.dtype, device=dev).uniform_(-2, 2, generator=gen)
+    host = torch.zeros((max(SMALL_CALL_BLOCKS),) + shape[1:], dtype=sh.dtype).pin_memory()
+    ref = _ref_module() if args.impl == "reference" else None
+    torch.cuda.synchronize()
+
+    def swap(src, dst, is_in):
+        if ref is not None:
+            ref.swap(src, dst, is_in, cache, host)
+        else:
+            ops.swap(src, dst, is_in, cache, host, mode=args.mode)
+
+    perm = workloads.randperm(sh.num_blocks, 7)
+    calls = max(args.steps, 1) * 20
+    cur = torch.cuda.current_stream(dev)
+    per_n, exact = {}, True
+    for n in SMALL_CALL_BLOCKS:
+        out_ids, in_ids, slots = perm[:n], perm[n:2 * n], list(range(n))
+        row = {}
+        for name, src, dst, is_in in (("out", out_ids, slots, False),
+                                      ("in", slots, in_ids, True)):
+            for _ in range(max(args.warmup, 3) * 20):
+                swap(src, dst, is_in)
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            t0 = time.perf_counter()
+            a.record(cur)
+            for _ in range(calls):
+                swap(src, dst, is_in)
+            b.record(cur)
+            wall = time.perf_counter() - t0
+            b.synchronize()
+            row[f"{name}_us"] = a.elapsed_time(b) * 1e3 / calls
+            row[f"{name}_host_us"] = wall * 1e6 / calls
+            if ref is None:
+                row[f"{name}_mode"] = _lib.last_mode_name()
+        exact &= torch.equal(cache[in_ids].view(torch.uint8), cache[out_ids].view(torch.uint8))
+        exact &= torch.equal(host[:n].to(dev).view(torch.uint8), cache[out_ids].view(torch.uint8))
+        per_n[str(n)] = row
+    value = (per_n["1"]["out_us"] + per_n["1"]["in_us"]) / 2
+    return {"impl": args.impl, "metric": "us per small swap call (n=1 block; table for n up "
+                                         "to 256)",
+            "value": value, "unit": "us", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": value / 1e3, "higher_is_better": False,
+            "dtype": "u8", "data": "synthetic: fp16 U(-2,2) from seed 0, seeded block ids",
+            "config": {"workload": "cfg2 K tensor [4096,16,32,128] fp16 (128 KiB blocks); "
+                                   "per n: one call moving n scattered blocks out to host "
+                                   "slots 0..n-1, one moving them back in to other blocks",
+                       "blocks_per_call": list(SMALL_CALL_BLOCKS),
+                       "calls_per_direction_and_n": calls,
+                       "api": "aegaeon.ops.swap (reference op)" if ref is not None
+                       else "aegaeon_b200.ops.swap -> kvx_swap",
+                       "transfer_mode": None if ref is not None else args.mode},
+            "per_n": per_n, "bit_exact": bool(exact),
+            "e2e": {"value": (per_n["1"]["out_host_us"] + per_n["1"]["in_host_us"]) / 2,
+                    "unit": "us", "h2d_bytes_per_step": sh.page_bytes,
+                    "d2h_bytes_per_step": sh.page_bytes}}
+
+
 def main():
     # Exactly one JSON line on stdout: libraries (NCCL prints its version)
     # write to fd 1 too, so fd 1 points at stderr while the benchmark runs and
@@ -1343,7 +1422,7 @@ def main():
     args = parse_args()
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
-        if args.config in (1, 4) and rank != 0:
+        if args.config in (1, 4, 7) and rank != 0:
             return
         if args.config == 3:
             if args.impl != "reference":
@@ -1357,7 +1436,7 @@ def main():
             if rank == 0:
                 emit(run_config6(args))
             return
-        fn = {1: run_config1, 4: run_config4, 5: run_config5}[args.config]
+        fn = {1: run_config1, 4: run_config4, 5: run_config5, 7: run_config7}[args.config]
         line = fn(args)
         if line is not None:
             emit(line)

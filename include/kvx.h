@@ -51,8 +51,11 @@ extern "C" {
 #define KVX_ERR_FORMAT 12          /* a file is not valid in its format        */
 
 /* ---- transfer modes (the `mode` argument of the copy entry points) ------- */
-#define KVX_MODE_AUTO 0     /* per-call choice by size and fragmentation       */
-#define KVX_MODE_SM 1       /* SM kernel, 16-byte vector loads/stores; host    */
+#define KVX_MODE_AUTO 0     /* per-call choice by size and fragmentation:      */
+                            /* at most 2 coalesced copies -> CE_EXTENT; host   */
+                            /* memory not mapped -> CE; payload >= 16 MiB with */
+                            /* mean host run >= 1 MiB -> CE; otherwise SM       */
+#define KVX_MODE_SM 1       /* SM kernel, 32-byte vector loads/stores; host    */
                             /* side through its device-mapped address          */
 #define KVX_MODE_CE 2       /* copy engines over coalesced runs; HBM side      */
                             /* gathered into / scattered from a staging area   */
@@ -262,8 +265,12 @@ int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream);
  * KVX_STAGING_BYTES, KVX_CE_PIPELINE=1 to double-buffer the staging area
  * (gather/scatter of one half on an internal stream while the copy engines
  * move the other; helps a single direction, hurts concurrent directions),
- * KVX_VEC_BYTES (32 default: 256-bit loads/stores where aligned; 16) and
- * KVX_BULK_CTAS_PER_SM (2 default; 1). */
+ * KVX_VEC_BYTES (32 default: 256-bit loads/stores where aligned; 16),
+ * KVX_BULK_CTAS_PER_SM (2 default; 1), KVX_CE_MIN_BYTES (16 MiB: smallest
+ * payload AUTO stages through the copy engines), KVX_DIRECT_MAX (2: most
+ * coalesced copies AUTO sends to the copy engines directly; 0 never) and
+ * KVX_INLINE (1: grid plans of at most 124 records travel in the kernel's
+ * parameters instead of through the descriptor ring; 0 never). */
 int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
                   int64_t ce_min_run, int64_t staging_bytes,
                   int64_t ce_pipeline /* -1 keep, 0 off, 1 on */);

@@ -4,6 +4,7 @@ import ctypes
 import os
 import re
 
+import pytest
 from conftest import ROOT
 
 
@@ -46,8 +47,6 @@ def test_extent_call_without_gpu(kvx):
 
 
 def test_missing_library_fails_loudly(monkeypatch, tmp_path):
-    import pytest
-
     from aegaeon_b200 import _lib
 
     monkeypatch.setattr(_lib, "_lib", None)
@@ -67,3 +66,63 @@ def test_id_arrays_from_any_sequence():
         assert list(a) == [3, 1, 2]
     assert len(_lib.i64_array([])) == 0
     assert len(_lib.i64_array(np.zeros(0, dtype=np.int64))) == 0
+
+
+def test_id_arrays_reject_non_int64_ids():
+    """An id that does not fit int64 or is not an integer raises instead of
+    wrapping around to some other block."""
+    import numpy as np
+
+    from aegaeon_b200 import _lib
+
+    assert list(_lib.i64_array(range(2, 12, 3))) == [2, 5, 8, 11]
+    assert list(_lib.i64_array([np.int64(7), 2**63 - 1, -1])) == [7, 2**63 - 1, -1]
+    for bad in ([2**63], [0, -2**63 - 1], list(range(20)) + [2**64]):
+        with pytest.raises(OverflowError):
+            _lib.i64_array(bad)
+    for bad in ([1.5], ["3"], [None]):
+        with pytest.raises(TypeError):
+            _lib.i64_array(bad)
+
+
+def test_call_shim_converts_ids_and_returns_status():
+    """The compiled call shim binds to libkvx.so without a GPU, takes ids as
+    lists, tuples or int64 buffers, raises on bad ids before calling the
+    library, and returns the library's status (here from its validation,
+    which runs before any CUDA call)."""
+    import numpy as np
+
+    from aegaeon_b200 import _lib
+
+    sh = _lib.shim()
+    assert sh is _lib.shim()
+    one_block = (0x10000, 4096, 4096, 0x200000, 4096, 0, 0)  # 1 cache block, 1 slot
+    assert sh.swap([], (), False, *one_block) == 0
+    for ids in ([3], (3,), np.array([3], dtype=np.int64), _lib.i64_array([3]),
+                np.array([3], dtype=np.int32)):
+        status = sh.swap(ids, [0], False, *one_block)
+        assert status == _lib.KVX_ERR_BLOCK_ID
+        with pytest.raises(IndexError, match="block id"):
+            _lib.check(status)
+    with pytest.raises(ValueError, match="1 ids but target_block_ids has 2"):
+        sh.swap([0], [0, 0], False, *one_block)
+    with pytest.raises(TypeError):
+        sh.swap([0.5], [0], False, *one_block)
+    with pytest.raises(OverflowError):
+        sh.swap([2**63], [0], False, *one_block)
+    big = list(range(100))  # beyond the shim's on-stack id buffer
+    assert sh.swap(big, big, True, *one_block) == _lib.KVX_ERR_BLOCK_ID
+
+
+def test_call_shim_swap_blocks_checks_lengths():
+    from aegaeon_b200 import _lib, swapper
+
+    page, blocks = 4096, 8
+    lay = swapper._Layout(0, [0x7f0000000000], [page], [blocks], [0], [1], [1],
+                          0x100000000, 4 * page, page, 0)
+    sh = _lib.shim()
+    with pytest.raises(ValueError, match="equal lengths"):
+        sh.swap_blocks(lay.handle, [0], [0], [0], [0], [], False, 0, 0)
+    status, copied, extents = sh.swap_blocks(lay.handle, [9], [0], [0], [0], [1], False, 0, 0)
+    assert status == _lib.KVX_ERR_BLOCK_ID and copied == 0 and extents == 0
+    lay.close()
