@@ -1,15 +1,18 @@
 // Copy kernels for KV-block movement on sm_100a.
 //
-// Both kernels walk a table of work items (kvx::Item: source, destination,
-// length, first tile).  The launch-wide tile sequence is split into one
+// Both kernels walk a work list: an item list (kvx::Item: source,
+// destination, length, first tile) or a grid list (entries x segments,
+// kvx_worklist.h).  The launch-wide tile sequence is split into one
 // contiguous span per CTA, so every CTA moves the same number of tiles and
-// streams through memory in order; a CTA finds its first item by binary search
-// and then advances item by item.
+// streams through memory in order; a CTA finds its first record by binary
+// search and then advances record by record.
 //
-//  * kvx_copy_vec  : 16-byte vector loads and stores, eight in flight per
-//                    thread (32 KiB per 256-thread CTA).  Works on any memory
-//                    the SM can address: local HBM, device-mapped page-locked
-//                    host memory (PCIe) and IPC-mapped peer HBM (NVLink).
+//  * kvx_copy_vec  : 32-byte vector loads and stores where source, destination
+//                    and length allow (16-byte and byte fallbacks), 128 bytes
+//                    in flight per thread (32 KiB per 256-thread CTA).  Works
+//                    on any memory the SM can address: local HBM,
+//                    device-mapped page-locked host memory (PCIe) and
+//                    IPC-mapped peer HBM (NVLink).
 //                    kvx_copy_vec_inline is the same kernel with a small grid
 //                    list passed by value in its parameters.
 //  * kvx_copy_bulk : local HBM only.  One elected thread runs a ring of TMA
