@@ -158,7 +158,8 @@ def shim():
                     "or `python -m aegaeon_b200.build`"
                 ) from e
             _kvxcall.bind(ctypes.cast(handle.kvx_swap, ctypes.c_void_p).value,
-                          ctypes.cast(handle.kvx_swap_blocks, ctypes.c_void_p).value)
+                          ctypes.cast(handle.kvx_swap_blocks, ctypes.c_void_p).value,
+                          ctypes.cast(handle.kvx_migrate_blocks, ctypes.c_void_p).value)
             _shim = _kvxcall
     return _shim
 

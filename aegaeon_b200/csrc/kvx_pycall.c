@@ -1,4 +1,5 @@
-/* Python call shim for the two per-request entry points of libkvx.so.
+/* Python call shim for the per-request entry points of libkvx.so (kvx_swap,
+ * kvx_swap_blocks, kvx_migrate_blocks).
  *
  * A swap issued for one decode turn moves a handful of blocks, and then the
  * cost of getting from Python to the C ABI is most of the call: ctypes
@@ -25,9 +26,13 @@ typedef int (*swap_fn)(const int64_t*, const int64_t*, int64_t, int, void*, uint
 typedef int (*swap_blocks_fn)(kvx_layout*, int64_t, const int64_t*, const int64_t*,
                               const int64_t*, const int64_t*, const int64_t*, int, int, void*,
                               uint64_t*, uint64_t*);
+typedef int (*migrate_blocks_fn)(kvx_layout*, kvx_layout*, int64_t, const int64_t*,
+                                 const int64_t*, const int64_t*, const int64_t*, const int64_t*,
+                                 int, void*, uint64_t*, uint64_t*);
 
 static swap_fn g_swap = NULL;
 static swap_blocks_fn g_swap_blocks = NULL;
+static migrate_blocks_fn g_migrate_blocks = NULL;
 
 /* Ids of one argument as an int64 array: borrowed from an int64 buffer, or
  * converted into `local` (when it fits) or a heap array. */
@@ -123,26 +128,27 @@ static int as_int(PyObject* o, int* v) {
   return 0;
 }
 
-/* bind(kvx_swap_address, kvx_swap_blocks_address) */
+/* bind(kvx_swap_address, kvx_swap_blocks_address, kvx_migrate_blocks_address) */
 static PyObject* py_bind(PyObject* self, PyObject* const* args, Py_ssize_t nargs) {
   (void)self;
-  if (nargs != 2) {
-    PyErr_SetString(PyExc_TypeError, "bind() takes 2 function addresses");
+  if (nargs != 3) {
+    PyErr_SetString(PyExc_TypeError, "bind() takes 3 function addresses");
     return NULL;
   }
-  uint64_t a, b;
-  if (as_u64(args[0], &a) || as_u64(args[1], &b)) return NULL;
-  if (!a || !b) {
+  uint64_t a, b, c;
+  if (as_u64(args[0], &a) || as_u64(args[1], &b) || as_u64(args[2], &c)) return NULL;
+  if (!a || !b || !c) {
     PyErr_SetString(PyExc_ValueError, "null function address");
     return NULL;
   }
   g_swap = (swap_fn)(uintptr_t)a;
   g_swap_blocks = (swap_blocks_fn)(uintptr_t)b;
+  g_migrate_blocks = (migrate_blocks_fn)(uintptr_t)c;
   Py_RETURN_NONE;
 }
 
 static int bound(void) {
-  if (g_swap && g_swap_blocks) return 1;
+  if (g_swap && g_swap_blocks && g_migrate_blocks) return 1;
   PyErr_SetString(PyExc_RuntimeError, "kvx call shim used before bind()");
   return 0;
 }
@@ -188,6 +194,47 @@ static PyObject* py_swap(PyObject* self, PyObject* const* args, Py_ssize_t nargs
   return PyLong_FromLong(rc);
 }
 
+/* The five entry lists of a segmented call (source, target, group, first,
+ * valid) from args[first_arg..first_arg+4], then one library call:
+ * `target` == 0 calls kvx_swap_blocks(source, ...), otherwise
+ * kvx_migrate_blocks(source, target, ...).  Returns (status, copied, extents). */
+static PyObject* entries_call(PyObject* const* args, int first_arg, uint64_t source,
+                              uint64_t target, int is_in, int mode, uint64_t stream) {
+  int64_t local[5][KVX_LOCAL_IDS];
+  Ids ids[5];
+  int got = 0;
+  for (; got < 5; ++got)
+    if (ids_from(args[first_arg + got], local[got], &ids[got])) break;
+  PyObject* result = NULL;
+  if (got == 5) {
+    if (ids[0].n != ids[1].n || ids[0].n != ids[2].n || ids[0].n != ids[3].n ||
+        ids[0].n != ids[4].n) {
+      PyErr_Format(PyExc_ValueError,
+                   "Swap block ids and metadata must have equal lengths: source=%zd, "
+                   "target=%zd, groups=%zd, first=%zd, valid=%zd",
+                   ids[0].n, ids[1].n, ids[2].n, ids[3].n, ids[4].n);
+    } else {
+      uint64_t copied = 0, extents = 0;
+      int rc;
+      Py_BEGIN_ALLOW_THREADS
+      if (target)
+        rc = g_migrate_blocks((kvx_layout*)(uintptr_t)source, (kvx_layout*)(uintptr_t)target,
+                              (int64_t)ids[0].n, ids[0].data, ids[1].data, ids[2].data,
+                              ids[3].data, ids[4].data, mode, (void*)(uintptr_t)stream,
+                              &copied, &extents);
+      else
+        rc = g_swap_blocks((kvx_layout*)(uintptr_t)source, (int64_t)ids[0].n, ids[0].data,
+                           ids[1].data, ids[2].data, ids[3].data, ids[4].data, is_in, mode,
+                           (void*)(uintptr_t)stream, &copied, &extents);
+      Py_END_ALLOW_THREADS
+      result = Py_BuildValue("(iKK)", rc, (unsigned long long)copied,
+                             (unsigned long long)extents);
+    }
+  }
+  for (int i = 0; i < got; ++i) ids_release(&ids[i]);
+  return result;
+}
+
 /* swap_blocks(layout, source_ids, target_ids, group_ids, first_kernel_blocks,
  *             valid_kernel_blocks, is_swap_in, mode, stream)
  *   -> (status, copied_bytes, copy_extents) */
@@ -204,33 +251,33 @@ static PyObject* py_swap_blocks(PyObject* self, PyObject* const* args, Py_ssize_
   if (is_in < 0) return NULL;
   if (as_u64(args[0], &layout) || as_int(args[7], &mode) || as_u64(args[8], &stream))
     return NULL;
-  int64_t local[5][KVX_LOCAL_IDS];
-  Ids ids[5];
-  int got = 0;
-  for (; got < 5; ++got)
-    if (ids_from(args[1 + got], local[got], &ids[got])) break;
-  PyObject* result = NULL;
-  if (got == 5) {
-    if (ids[0].n != ids[1].n || ids[0].n != ids[2].n || ids[0].n != ids[3].n ||
-        ids[0].n != ids[4].n) {
-      PyErr_Format(PyExc_ValueError,
-                   "Swap block ids and metadata must have equal lengths: source=%zd, "
-                   "target=%zd, groups=%zd, first=%zd, valid=%zd",
-                   ids[0].n, ids[1].n, ids[2].n, ids[3].n, ids[4].n);
-    } else {
-      uint64_t copied = 0, extents = 0;
-      int rc;
-      Py_BEGIN_ALLOW_THREADS
-      rc = g_swap_blocks((kvx_layout*)(uintptr_t)layout, (int64_t)ids[0].n, ids[0].data,
-                         ids[1].data, ids[2].data, ids[3].data, ids[4].data, is_in, mode,
-                         (void*)(uintptr_t)stream, &copied, &extents);
-      Py_END_ALLOW_THREADS
-      result = Py_BuildValue("(iKK)", rc, (unsigned long long)copied,
-                             (unsigned long long)extents);
-    }
+  if (!layout) {
+    PyErr_SetString(PyExc_ValueError, "null layout");
+    return NULL;
   }
-  for (int i = 0; i < got; ++i) ids_release(&ids[i]);
-  return result;
+  return entries_call(args, 1, layout, 0, is_in, mode, stream);
+}
+
+/* migrate_blocks(source_layout, target_layout, source_ids, target_ids,
+ *                group_ids, first_kernel_blocks, valid_kernel_blocks, mode,
+ *                stream) -> (status, copied_bytes, copy_extents) */
+static PyObject* py_migrate_blocks(PyObject* self, PyObject* const* args, Py_ssize_t nargs) {
+  (void)self;
+  if (nargs != 9) {
+    PyErr_SetString(PyExc_TypeError, "migrate_blocks() takes 9 arguments");
+    return NULL;
+  }
+  if (!bound()) return NULL;
+  uint64_t source, target, stream;
+  int mode;
+  if (as_u64(args[0], &source) || as_u64(args[1], &target) || as_int(args[7], &mode) ||
+      as_u64(args[8], &stream))
+    return NULL;
+  if (!source || !target) {
+    PyErr_SetString(PyExc_ValueError, "null layout");
+    return NULL;
+  }
+  return entries_call(args, 2, source, target, 0, mode, stream);
 }
 
 static PyMethodDef kMethods[] = {
@@ -240,6 +287,8 @@ static PyMethodDef kMethods[] = {
      "kvx_swap with ids from Python sequences; returns the status"},
     {"swap_blocks", (PyCFunction)(void (*)(void))py_swap_blocks, METH_FASTCALL,
      "kvx_swap_blocks with ids from Python sequences; returns (status, copied, extents)"},
+    {"migrate_blocks", (PyCFunction)(void (*)(void))py_migrate_blocks, METH_FASTCALL,
+     "kvx_migrate_blocks with ids from Python sequences; returns (status, copied, extents)"},
     {NULL, NULL, 0, NULL},
 };
 

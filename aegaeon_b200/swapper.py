@@ -466,9 +466,11 @@ class KVSwapper:
             first_kernel_blocks = [0] * n
         if valid_kernel_blocks is None:
             valid_kernel_blocks = [self.group_ratios[g] for g in group_ids]
-        n, src, dst, grp, first, valid = _entry_arrays(
-            source_block_ids, target_block_ids, group_ids, first_kernel_blocks,
-            valid_kernel_blocks)
+        _check_lengths(source_block_ids, target_block_ids, group_ids, first_kernel_blocks,
+                       valid_kernel_blocks)
+        a = _lib.ids_arg
+        src, dst, grp, first, valid = (a(source_block_ids), a(target_block_ids), a(group_ids),
+                                       a(first_kernel_blocks), a(valid_kernel_blocks))
         peer_layout = self._peers[source_engine_id][0]
         if direction == "pull":
             s_layout, t_layout = peer_layout, self.local_endpoint()
@@ -480,18 +482,17 @@ class KVSwapper:
             stream = self.swap_in_stream
         new_event = torch.cuda.Event()
         self._wait_source_events(stream, new_event, request_ids, source_events)
-        copied = ctypes.c_uint64(0)
-        extents = ctypes.c_uint64(0)
-        with torch.cuda.device(self.device):
-            _lib.check(
-                _lib.lib().kvx_migrate_blocks(
-                    s_layout.handle, t_layout.handle, n, src, dst, grp, first, valid,
-                    _lib.mode_of(mode), stream.cuda_stream, ctypes.byref(copied),
-                    ctypes.byref(extents),
-                )
-            )
-            new_event.record(stream)
-        self.last_stats = (copied.value, extents.value)
+        args = (s_layout.handle, t_layout.handle, src, dst, grp, first, valid,
+                _lib.mode_of(mode), stream.cuda_stream)
+        if torch.cuda.current_device() == self.device_index:
+            status, copied, extents = _lib.shim().migrate_blocks(*args)
+        else:
+            with torch.cuda.device(self.device_index):
+                status, copied, extents = _lib.shim().migrate_blocks(*args)
+        if status:
+            _lib.check(status)
+        new_event.record(stream)
+        self.last_stats = (copied, extents)
         return new_event
 
     def copy_blocks_local(self, source_block_ids, target_block_ids, *, mode="auto",
@@ -500,15 +501,19 @@ class KVSwapper:
         migration; HBM bound).  Overlapping source / target ids are ordered
         as a sequential loop would order them."""
         n = len(source_block_ids)
+        if len(target_block_ids) != n:
+            raise ValueError(f"source_block_ids has {n} ids but target_block_ids has "
+                             f"{len(target_block_ids)}")
         ep = self.local_endpoint()
-        n, src, dst, grp, first, valid = _entry_arrays(
-            source_block_ids, target_block_ids, [0] * n, [0] * n, [self.group_ratios[0]] * n)
         stream = stream or torch.cuda.current_stream(self.device)
         ev = torch.cuda.Event()
-        with torch.cuda.device(self.device):
-            _lib.check(_lib.lib().kvx_migrate_blocks(
-                ep.handle, ep.handle, n, src, dst, grp, first, valid, _lib.mode_of(mode),
-                stream.cuda_stream, None, None))
+        args = (ep.handle, ep.handle, _lib.ids_arg(source_block_ids),
+                _lib.ids_arg(target_block_ids), [0] * n, [0] * n, [self.group_ratios[0]] * n,
+                _lib.mode_of(mode), stream.cuda_stream)
+        with torch.cuda.device(self.device_index):
+            status, _, _ = _lib.shim().migrate_blocks(*args)
+            if status:
+                _lib.check(status)
             ev.record(stream)
         return ev
 

@@ -494,6 +494,9 @@ def cpu_baseline(seconds: float) -> dict:
                       f"2 GiB host cache, {threads} threads, {dt:.1f} s; cpu {cpu}"}
 
 
+MIGRATION_SMALL_BLOCKS = (1, 4, 16, 64)
+
+
 def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull") -> dict:
     """Configuration 3 at N >= 2: pairs (i, i + N/2), rank i the prefill side.
     pull: the decode rank maps the prefill rank's cache and copies the blocks
@@ -542,6 +545,30 @@ def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull"
     b.synchronize()
     t = dist_.max(a.elapsed_time(b) / 1e3)
     dist_.barrier()
+    # Small calls: the plan's first n blocks (all 56 segments), as a decode
+    # rank pulls a short request; µs per call, device time, max over ranks.
+    # The same source/target pairs as the plan, so the parity check below
+    # still holds.
+    small = {}
+    for n in MIGRATION_SMALL_BLOCKS:
+        sub_src, sub_dst = plan.source_ids[:n], plan.target_ids[:n]
+
+        def one():
+            if active:
+                sw.migrate_blocks([pair], partner, sub_src, sub_dst, None,
+                                  direction=direction, stream=stream)
+
+        for _ in range(20):
+            one()
+        stream.synchronize()
+        dist_.barrier()
+        a.record(stream)
+        for _ in range(200):
+            one()
+        b.record(stream)
+        b.synchronize()
+        small[str(n)] = dist_.max(a.elapsed_time(b) * 1e3 / 200)
+        dist_.barrier()
     # Parity of the timed push: the decode rank's blocks equal the prefill
     # rank's (checked on a digest of the moved pages, both sides on device).
     moved = [p.view(-1, sh.page_bytes)[plan.source_ids if is_src else plan.target_ids]
@@ -565,6 +592,10 @@ def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull"
             "per_pair_gbs": per_pair, "nvlink_peer_copy_gbs": 770.0,
             "frac_of_measured_peer_copy": per_pair / 770.0, "frac_of_nominal_900": per_pair / 900.0,
             "ms_per_step": t / steps * 1e3, "bit_exact": parity,
+            "small_calls_us": small,
+            "small_calls_how": "per n: one migrate_blocks call moving n blocks x 56 segments "
+                               f"({sh.composite_bytes // 1024} KiB per block), 200 calls "
+                               "after 20 warm-up, CUDA events, max over ranks",
             "nccl_sendrecv": {"value": half * nbytes / nccl / 1e9, "unit": "GB/s",
                               "per_pair_gbs": nbytes / nccl / 1e9,
                               "how": "gather blocks into a contiguous buffer (kvx kernel), "

@@ -125,4 +125,11 @@ def test_call_shim_swap_blocks_checks_lengths():
         sh.swap_blocks(lay.handle, [0], [0], [0], [0], [], False, 0, 0)
     status, copied, extents = sh.swap_blocks(lay.handle, [9], [0], [0], [0], [1], False, 0, 0)
     assert status == _lib.KVX_ERR_BLOCK_ID and copied == 0 and extents == 0
+    # migration between two layouts: same checks, validation before any CUDA call
+    with pytest.raises(ValueError, match="equal lengths"):
+        sh.migrate_blocks(lay.handle, lay.handle, [0, 1], [2], [0], [0], [1], 0, 0)
+    with pytest.raises(ValueError, match="null layout"):
+        sh.migrate_blocks(lay.handle, 0, [0], [2], [0], [0], [1], 0, 0)
+    status, _, _ = sh.migrate_blocks(lay.handle, lay.handle, [0], [blocks], [0], [0], [1], 0, 0)
+    assert status == _lib.KVX_ERR_BLOCK_ID
     lay.close()
