@@ -363,6 +363,26 @@ class SwapBench:
         b.synchronize()
         return a.elapsed_time(b) / 1e3
 
+    def live_one_direction(self, lists, mode: str) -> tuple:
+        """Swap-out steps alone (nothing on the swap-in stream), with kernel
+        timing on: the staging kernel's live launch duration without the other
+        direction's kernels and copy-engine DMA beside it.  Returns
+        kvx_kernel_timing_read's (launches, total ms, busy ms, bytes)."""
+        from aegaeon_b200 import _lib
+
+        n = self.per_dir
+        z, one = [0] * n, [1] * n
+        self.s_out.synchronize()
+        self.s_in.synchronize()
+        _lib.kernel_timing_read()
+        _lib.kernel_timing(True)
+        for out_ids, rows_out, _, _ in lists:
+            self.sw.swap_blocks([0], out_ids, rows_out, z, z, one, [None], False, mode=mode,
+                                stream=self.s_out)
+        self.s_out.synchronize()
+        _lib.kernel_timing(False)
+        return _lib.kernel_timing_read()
+
     def timed_e2e(self, steps: int, mode: str):
         """Wall clock through the public API from block tables."""
         from aegaeon_b200 import block_table as bt
@@ -708,6 +728,7 @@ def run_kvx(args):
     t_e2e = dist_.max(bench.timed_e2e(args.steps, args.mode))
     kr = bench.kernel_roofline(mode_bulk=True)
     kr_vec = bench.kernel_roofline(mode_bulk=False)
+    one_dir = bench.live_one_direction(lists[args.warmup:args.warmup + 2], args.mode)
     bytes_total = bench.bytes_per_step * args.steps * dist_.world
     value = bytes_total / t_dev / 1e9
     e2e = bytes_total / t_e2e / 1e9
@@ -774,6 +795,16 @@ def run_kvx(args):
                 "algorithmic_bytes_per_launch": (k_bytes // k_launches) if k_launches else None,
                 "mean_launch_ms": (k_ms / k_launches) if k_launches else None,
                 "busy_ms": k_busy_ms,
+                "one_direction_live": {
+                    "how": "2 swap-out steps with nothing on the swap-in stream, same events "
+                           "and byte count: the launches without the other direction beside "
+                           "them",
+                    "launches": one_dir[0],
+                    "mean_launch_ms": (one_dir[1] / one_dir[0]) if one_dir[0] else None,
+                    "achieved": (one_dir[3] / (one_dir[1] / 1e3) / 1e9) if one_dir[1] else None,
+                    "frac": (one_dir[3] / (one_dir[1] / 1e3) / 1e9 / hbm_peak)
+                    if one_dir[1] else None,
+                },
                 "isolated_bulk_gbs": kr["algorithmic_bytes"] / kr["seconds"] / 1e9,
                 "isolated_vec_gbs": kr_vec["algorithmic_bytes"] / kr_vec["seconds"] / 1e9,
                 "ncu": "profiles/kvx_copy_bulk_grid_cfg2_small.md",
