@@ -1,8 +1,8 @@
 """Generate golden fixtures by running the reference's own Python code.
 
-Run in a container that has the Aegaeon checkout (default /root/reference,
-override with AEGAEON_REFERENCE); the fixtures it writes are committed and the
-tests never read the checkout.  Nothing is written into the checkout (the
+Run where an Aegaeon checkout is present (its directory is the
+AEGAEON_REFERENCE environment variable, or REF's default below); the fixtures
+it writes are committed and the tests never read the checkout.  Nothing is written into the checkout (the
 reference logger writes ``output.log`` into the working directory, so this
 script runs from a temporary one).
 
