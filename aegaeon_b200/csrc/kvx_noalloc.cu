@@ -116,22 +116,41 @@ int kvx_swap_noalloc(const int64_t* source_block_ids, const int64_t* target_bloc
     if (slot < 0 || uint64_t(slot) >= swap_blocks)
       return fail(KVX_ERR_BLOCK_ID, "kv_swap block id out of range");
   }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The ids travel through static host storage that the next call reuses, so
+  // a copy recorded into a graph would read whatever a later call left there:
+  // a capturing stream is refused before anything is queued.
+  cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+  cudaError_t e = cudaStreamIsCapturing(s, &capture);
+  if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "cudaStreamIsCapturing failed");
+  if (capture != cudaStreamCaptureStatusNone)
+    return fail(KVX_ERR_INVALID_ARGUMENT,
+                "kvx_swap_noalloc: the stream is capturing; call it on a stream that is not");
   int device = 0;
-  cudaError_t e = cudaGetDevice(&device);
+  e = cudaGetDevice(&device);
   if (e != cudaSuccess) return fail(KVX_ERR_CUDA, "cudaGetDevice failed");
+  // Memory kinds as kvx_swap accepts them: the cache in device or managed
+  // memory of this device, the host side page-locked and mapped, or managed.
   cudaPointerAttributes ca, ha;
   if (cudaPointerGetAttributes(&ca, kv_cache) != cudaSuccess ||
-      ca.type != cudaMemoryTypeDevice || ca.device != device) {
+      !(ca.type == cudaMemoryTypeManaged ||
+        (ca.type == cudaMemoryTypeDevice && ca.device == device))) {
     cudaGetLastError();
-    return fail(KVX_ERR_INVALID_ARGUMENT, "kv_cache is not device memory of the current device");
+    return fail(KVX_ERR_INVALID_ARGUMENT,
+                "kv_cache is not device (or managed) memory of the current device");
   }
-  if (cudaPointerGetAttributes(&ha, kv_swap) != cudaSuccess || ha.type != cudaMemoryTypeHost ||
-      !ha.devicePointer) {
+  uint64_t host_dev = 0;
+  if (cudaPointerGetAttributes(&ha, kv_swap) != cudaSuccess) {
     cudaGetLastError();
+  } else if (ha.type == cudaMemoryTypeHost && ha.devicePointer) {
+    host_dev = reinterpret_cast<uint64_t>(ha.devicePointer);
+  } else if (ha.type == cudaMemoryTypeManaged) {
+    host_dev = reinterpret_cast<uint64_t>(kv_swap);
+  }
+  if (!host_dev)
     return fail(KVX_ERR_HOST_MEMORY,
                 "kv_swap must be page-locked host memory mapped for the device "
-                "(cudaHostAlloc or cudaHostRegister)");
-  }
+                "(cudaHostAlloc or cudaHostRegister) or managed memory");
   const uint32_t tiles_per_block = uint32_t((block_bytes + (1u << kTileShift) - 1) >> kTileShift);
   if (uint64_t(num_ids) * tiles_per_block > 0xffffffffull)
     return fail(KVX_ERR_INVALID_ARGUMENT, "request too large for one call");
@@ -152,8 +171,10 @@ int kvx_swap_noalloc(const int64_t* source_block_ids, const int64_t* target_bloc
     g_upload[kMaxIds + m] = g_pairs[k].target;
     ++m;
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // The host arrays are pageable: the copy has consumed them when it returns.
+  // g_upload is pageable.  The runtime's documented behaviour for an
+  // asynchronous copy from pageable host memory to the device is to copy the
+  // source into its own staging memory before the call returns, so g_upload
+  // may be rewritten by the next call as soon as these return.
   e = cudaMemcpyAsync(scratch, g_upload, size_t(m) * sizeof(int64_t), cudaMemcpyHostToDevice, s);
   if (e == cudaSuccess)
     e = cudaMemcpyAsync(scratch + kMaxIds, g_upload + kMaxIds, size_t(m) * sizeof(int64_t),
@@ -163,7 +184,6 @@ int kvx_swap_noalloc(const int64_t* source_block_ids, const int64_t* target_bloc
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
   const uint32_t grid = uint32_t(std::min<uint64_t>(tiles, uint64_t(sms)));
-  const uint64_t host_dev = reinterpret_cast<uint64_t>(ha.devicePointer);
   const uint64_t cache = reinterpret_cast<uint64_t>(kv_cache);
   if (is_swap_in)
     kvx_copy_ids<kSrcHost><<<grid, kVecThreads, 0, s>>>(scratch, uint32_t(m), block_bytes,

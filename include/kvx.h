@@ -294,7 +294,10 @@ int kvx_safetensors_meta_json(const char* file_path, char* out,
  * arena, a process swapping out near its memory limit during a model switch,
  * or code where an allocation would synchronise the device.  Same copy as
  * kvx_swap in its SM zero-copy mode (kv_swap must be page-locked and mapped
- * for the device), same checks, same last-writer rule for repeated targets.
+ * for the device, or managed memory), same checks, same last-writer rule for
+ * repeated targets.  A stream that is capturing is refused with
+ * KVX_ERR_INVALID_ARGUMENT before anything is queued: the ids go to the
+ * device through static host storage that the next call rewrites.
  * Its scratch is a fixed device array of KVX_NOALLOC_MAX_IDS source and
  * target ids (1 MiB), compiled into the library and held by every GPU that
  * loads it until the process exits; more ids per call are rejected with

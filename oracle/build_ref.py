@@ -20,7 +20,10 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REF_DIR = os.path.join(HERE, "_ref")
-DEFAULT_REFERENCE = os.environ.get("AEGAEON_REFERENCE", "/root/reference")
+# The Aegaeon checkout: AEGAEON_REFERENCE, else a directory named "reference"
+# beside this repository's root.
+DEFAULT_REFERENCE = os.environ.get(
+    "AEGAEON_REFERENCE", os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 
 def built_module_path() -> str | None:

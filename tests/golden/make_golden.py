@@ -1,7 +1,8 @@
 """Generate golden fixtures by running the reference's own Python code.
 
 Run where an Aegaeon checkout is present (its directory is the
-AEGAEON_REFERENCE environment variable, or REF's default below); the fixtures
+AEGAEON_REFERENCE environment variable, else a directory named
+``reference`` beside the repository root); the fixtures
 it writes are committed and the tests never read the checkout.  Nothing is written into the checkout (the
 reference logger writes ``output.log`` into the working directory, so this
 script runs from a temporary one).
@@ -33,8 +34,12 @@ import types
 
 import numpy as np
 
-REF = os.environ.get("AEGAEON_REFERENCE", "/root/reference")
 OUT = os.path.dirname(os.path.abspath(__file__))
+# The Aegaeon checkout: AEGAEON_REFERENCE, else a directory named "reference"
+# beside this repository's root (tests/golden -> tests -> repo -> its parent).
+REF = os.environ.get("AEGAEON_REFERENCE",
+                     os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(OUT))),
+                                  "reference"))
 
 
 def stub_ray() -> None:

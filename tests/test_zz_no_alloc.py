@@ -8,8 +8,10 @@ call) is a fixed device array inside the library instead of memory the library
 allocates.  This test calls it through the C ABI and compares what it writes
 with what the regular entry point kvx_swap writes, bit for bit (the tolerance
 of every swap test: these are byte copies), on two calls in a row.  It also
-checks that those calls leave the device's free memory unchanged and that a
-request above the array's capacity is refused.
+checks that those calls leave the device's free memory unchanged, that a
+request above the array's capacity and a call on a capturing stream are
+refused, and that managed memory is accepted on both sides as kvx_swap accepts
+it.
 
 The file name makes pytest collect it last, so a run that stops at the first
 failure has run every other test before it.
@@ -17,6 +19,7 @@ failure has run every other test before it.
 
 import ctypes
 
+import numpy as np
 import pytest
 import torch
 
@@ -96,3 +99,76 @@ def test_noalloc_refuses_more_ids_than_its_scratch_holds():
     assert b"KVX_NOALLOC_MAX_IDS" in _lib.lib().kvx_last_error()
     torch.cuda.synchronize()
     assert int(host.view(torch.int16).abs().sum()) == 0
+
+
+def test_noalloc_refuses_a_capturing_stream():
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    cache = torch.ones((4, 1024), dtype=torch.float16, device=dev)
+    host = torch.zeros((4, 1024), dtype=torch.float16).pin_memory()
+    # the one-time set-up call, outside any capture
+    assert noalloc([0], [1], False, cache, host) == 0, _lib.lib().kvx_last_error()
+    torch.cuda.synchronize()
+    host.zero_()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    with torch.cuda.stream(side):
+        graph.capture_begin()
+        try:
+            rc = noalloc([0, 1], [2, 3], False, cache, host)
+            msg = _lib.lib().kvx_last_error()
+        finally:
+            graph.capture_end()
+    assert rc == _lib.KVX_ERR_INVALID_ARGUMENT
+    assert b"capturing" in msg
+    torch.cuda.synchronize()
+    assert int(host.view(torch.int16).abs().sum()) == 0
+
+
+def _cudart():
+    for name in ("libcudart.so.12", "libcudart.so"):
+        try:
+            return ctypes.CDLL(name)
+        except OSError:
+            continue
+    pytest.skip("no CUDA runtime library to allocate managed memory with")
+
+
+def test_noalloc_accepts_managed_memory_like_kvx_swap():
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    rt = _cudart()
+    rt.cudaMallocManaged.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_size_t,
+                                     ctypes.c_uint]
+    rt.cudaFree.argtypes = [ctypes.c_void_p]
+    blocks, slots, block = 32, 24, 16 * 8 * 128 * 2
+    cache_m, host_m = ctypes.c_void_p(), ctypes.c_void_p()
+    assert rt.cudaMallocManaged(ctypes.byref(cache_m), blocks * block, 1) == 0
+    assert rt.cudaMallocManaged(ctypes.byref(host_m), slots * block, 1) == 0
+    try:
+        content = np.random.default_rng(23).integers(0, 256, blocks * block, dtype=np.uint8)
+        torch.cuda.synchronize()
+        ctypes.memmove(cache_m.value, content.ctypes.data, blocks * block)
+        ctypes.memset(host_m.value, 0, slots * block)
+        cpu = torch.Generator().manual_seed(24)
+        src = torch.randperm(blocks, generator=cpu)[:slots].tolist()
+        dst = torch.randperm(slots, generator=cpu).tolist()
+        stream = torch.cuda.current_stream().cuda_stream
+        rc = _lib.lib().kvx_swap_noalloc(ids(src), ids(dst), len(src), 0, cache_m.value,
+                                         blocks * block, block, host_m.value, slots * block,
+                                         stream)
+        assert rc == 0, _lib.lib().kvx_last_error()
+        # the regular entry point on ordinary device / page-locked buffers
+        cache = torch.from_numpy(content).to(dev).view(blocks, block)
+        host = torch.zeros((slots, block), dtype=torch.uint8).pin_memory()
+        rc = _lib.lib().kvx_swap(ids(src), ids(dst), len(src), 0, cache.data_ptr(),
+                                 blocks * block, block, host.data_ptr(), slots * block,
+                                 _lib.MODE_SM, stream)
+        assert rc == 0, _lib.lib().kvx_last_error()
+        torch.cuda.synchronize()
+        got = np.ctypeslib.as_array((ctypes.c_uint8 * (slots * block)).from_address(host_m.value))
+        assert np.array_equal(got, host.numpy().reshape(-1))
+    finally:
+        torch.cuda.synchronize()
+        rt.cudaFree(cache_m)
+        rt.cudaFree(host_m)
