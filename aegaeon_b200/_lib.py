@@ -82,6 +82,8 @@ SIGNATURES = {
     "kvx_stream_wait_events": (_int, [_vp, ctypes.POINTER(_vp), _i64]),
     "kvx_event_release": (_int, [_vp]),
     "kvx_upload_chunked": (_int, [_vp, _vp, _u64, _u64, _vp]),
+    "kvx_upload_weights": (_int, [ctypes.POINTER(_vp), ctypes.POINTER(_vp), _p_u64, _i64, _u64,
+                                  _int, _vp]),
     "kvx_byte_extent": (_int, [_u64, _i64, _i64, _i64, _p_u64, _p_u64]),
     "kvx_plan_swap_blocks": (
         _int,

@@ -24,6 +24,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/kvx.h"
@@ -147,6 +148,13 @@ struct DeviceState {
   std::vector<cudaEvent_t> pool;
   Staging staging[2];  // [0] device->host, [1] host->device
   bool bulk_ready = false;
+  // Weight upload from pageable memory: two page-locked bounce buffers, each
+  // guarded by the event recorded after the copy that last read it.
+  std::mutex upload_mu;
+  char* bounce[2] = {nullptr, nullptr};
+  size_t bounce_cap = 0;
+  cudaEvent_t bounce_ev[2] = {nullptr, nullptr};
+  bool bounce_used[2] = {false, false};
 };
 
 std::mutex g_dev_mu;
@@ -938,6 +946,59 @@ int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
   return rc;
 }
 
+// ---- weight upload (model switch) ------------------------------------------
+
+// memcpy split over `threads` host threads (the calling thread takes a share).
+void parallel_memcpy(char* dst, const char* src, size_t n, int threads) {
+  constexpr size_t kMinShare = size_t(4) << 20;
+  threads = int(std::max<size_t>(1, std::min<size_t>(size_t(std::max(threads, 1)),
+                                                      n / kMinShare)));
+  if (threads == 1) {
+    std::memcpy(dst, src, n);
+    return;
+  }
+  const size_t share = (n / threads + 4095) & ~size_t(4095);
+  std::vector<std::thread> pool;
+  pool.reserve(threads - 1);
+  for (int t = 1; t < threads; ++t) {
+    const size_t a = std::min(n, t * share), b = std::min(n, (t + 1) * share);
+    if (a < b) pool.emplace_back([=] { std::memcpy(dst + a, src + a, b - a); });
+  }
+  std::memcpy(dst, src, std::min(n, share));
+  for (std::thread& th : pool) th.join();
+}
+
+int bounce_ready(DeviceState* st, size_t want) {
+  if (st->bounce_cap >= want) return KVX_OK;
+  for (int b = 0; b < 2; ++b) {
+    if (st->bounce_used[b]) KVX_CUDA(cudaEventSynchronize(st->bounce_ev[b]));
+    if (st->bounce[b]) cudaFreeHost(st->bounce[b]);
+    st->bounce[b] = nullptr;
+    st->bounce_used[b] = false;
+  }
+  st->bounce_cap = 0;
+  for (int b = 0; b < 2; ++b) {
+    cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&st->bounce[b]), want,
+                                  cudaHostAllocDefault);
+    if (e != cudaSuccess) return cuda_error(e, "cudaHostAlloc(upload bounce buffer)");
+    if (!st->bounce_ev[b])
+      KVX_CUDA(cudaEventCreateWithFlags(&st->bounce_ev[b], cudaEventDisableTiming));
+  }
+  st->bounce_cap = want;
+  return KVX_OK;
+}
+
+// Page-locked or device-addressable host source: the copy engine reads it
+// directly.
+bool host_is_pinned(const void* p) {
+  cudaPointerAttributes a;
+  if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  return a.type == cudaMemoryTypeHost || a.type == cudaMemoryTypeManaged;
+}
+
 }  // namespace
 
 // Sets the message kvx_last_error() returns to this thread (used by the
@@ -1432,6 +1493,64 @@ int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,
     KVX_CUDA(cudaMemcpyAsync(static_cast<char*>(dst_device) + o,
                              static_cast<const char*>(src_host) + o, n,
                              cudaMemcpyHostToDevice, s));
+  }
+  return KVX_OK;
+}
+
+int kvx_upload_weights(void* const* dst_device, const void* const* src_host,
+                       const uint64_t* bytes, int64_t num_buffers, uint64_t chunk_bytes,
+                       int host_threads, void* stream) {
+  t_last_error.clear();
+  if (num_buffers < 0) return set_error(KVX_ERR_INVALID_ARGUMENT, "negative buffer count");
+  if (num_buffers == 0) return KVX_OK;
+  if (!dst_device || !src_host || !bytes)
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "null array argument");
+  if (chunk_bytes == 0) return set_error(KVX_ERR_INVALID_ARGUMENT, "chunk_bytes must be > 0");
+  int device = 0;
+  KVX_CUDA(cudaGetDevice(&device));
+  std::vector<bool> pinned(static_cast<size_t>(num_buffers), false);
+  bool any_pageable = false;
+  for (int64_t i = 0; i < num_buffers; ++i) {
+    if (bytes[i] == 0) continue;
+    if (!dst_device[i] || !src_host[i])
+      return set_error(KVX_ERR_INVALID_ARGUMENT, "null buffer " + std::to_string(i));
+    int rc = check_device_memory(dst_device[i], device, "destination buffer");
+    if (rc) return rc;
+    pinned[size_t(i)] = host_is_pinned(src_host[i]);
+    any_pageable |= !pinned[size_t(i)];
+  }
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  DeviceState* st = nullptr;
+  if (any_pageable) {
+    int rc = get_state(device, &st);
+    if (rc) return rc;
+  }
+  std::unique_lock<std::mutex> lock;
+  if (st) {
+    lock = std::unique_lock<std::mutex>(st->upload_mu);
+    int rc = bounce_ready(st, size_t(chunk_bytes));
+    if (rc) return rc;
+  }
+  int next = 0;  // bounce buffer of the next pageable chunk
+  for (int64_t i = 0; i < num_buffers; ++i) {
+    char* dst = static_cast<char*>(dst_device[i]);
+    const char* src = static_cast<const char*>(src_host[i]);
+    for (uint64_t o = 0; o < bytes[i]; o += chunk_bytes) {
+      const uint64_t n = std::min(chunk_bytes, bytes[i] - o);
+      if (pinned[size_t(i)]) {
+        KVX_CUDA(cudaMemcpyAsync(dst + o, src + o, n, cudaMemcpyHostToDevice, s));
+        continue;
+      }
+      // The host fills one bounce buffer while the copy engine drains the
+      // other; a buffer is refilled once the copy that read it has finished.
+      const int b = next;
+      next ^= 1;
+      if (st->bounce_used[b]) KVX_CUDA(cudaEventSynchronize(st->bounce_ev[b]));
+      parallel_memcpy(st->bounce[b], src + o, size_t(n), host_threads);
+      KVX_CUDA(cudaMemcpyAsync(dst + o, st->bounce[b], n, cudaMemcpyHostToDevice, s));
+      KVX_CUDA(cudaEventRecord(st->bounce_ev[b], s));
+      st->bounce_used[b] = true;
+    }
   }
   return KVX_OK;
 }

@@ -15,16 +15,22 @@ Printed JSON line (rank 0): ``value`` is the device-timed box aggregate GB/s
 (CUDA events on the launching streams, max over ranks); ``e2e`` is the same
 metric timed by the wall clock through the public API from block tables
 (plan_swap_lists -> KVSwapper.swap_blocks -> wait), with the payload crossing
-the host link inside the timed region.  ``roofline`` is the binding host link
-(measured copy-engine peak, both directions together); ``kernel_roofline`` the
-device-side gather kernel against the measured HBM copy peak.  At N >= 2 a
-``migration`` object adds configuration 3 (NVLink P->D migration, pairs
-(i, i+N/2)).
+the host link inside the timed region.  ``roofline`` is the device-side
+gather kernel against the measured HBM copy peak, with the binding host-link
+roofline nested in it (``roofline.host_link``: the measured concurrent
+copy-engine peak of all GPUs of the run and the host DRAM copy bandwidth).
+At N=1 the line ends with ``baseline_configs``: configurations 1, 4 and 5,
+both arms, each checked byte for byte.  At N >= 2 the ``migration`` (pull)
+and ``migration_push`` objects add configuration 3 (NVLink P->D migration,
+pairs (i, i+N/2)) with an exact cross-GPU comparison and a measured
+peer-copy peak, and ``migration_summary`` ends the line.
 
 ``--impl reference`` times the reference's own swap op (ops/swap.cu, built
-from the reference sources into oracle/_ref) on the same configuration: one
-call per K or V tensor, one cudaMemcpyAsync per block, out and in on two
-streams.  Under torchrun only rank 0 runs it.
+from the reference sources into oracle/_ref) on the same configuration and
+the same ``config`` object: one call per K or V tensor, one cudaMemcpyAsync
+per block, out and in on two streams.  Under torchrun every rank runs it on
+its own GPU (one reference Worker per GPU) and the box aggregate uses the
+slowest rank's time.
 """
 
 from __future__ import annotations
@@ -75,6 +81,8 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-migration", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="N=1: skip the configuration 1/4/5 objects of the default line")
     p.add_argument("--migration-direction", choices=["pull", "push"], default="pull",
                    help="pull: the decode rank copies from the prefill rank's mapped cache "
                         "(the reference's decode-side migrate_blocks); push: the prefill "
@@ -310,6 +318,7 @@ class SwapBench:
             [((f"layer{i // 2}.{'kv'[i % 2]}",), sh.num_blocks * sh.page_bytes)
              for i in range(sh.num_segments)], sh.num_blocks)
         self.comp = comp
+        self.segments = segments
         self.rows = 2 * blocks_per_dir
         self.pool = torch.empty(self.rows * comp, dtype=torch.uint8).pin_memory()
         # rows [per_dir, 2*per_dir) hold earlier swapped-out blocks (random bytes)
@@ -463,61 +472,244 @@ class SwapBench:
         self.sw.close()
 
 
-def cpu_baseline(seconds: float) -> dict:
-    """The same block gather on the host cores (CPU restatement of the copy,
-    multi-threaded), on a bounded sample."""
-    import numpy as np
+def host_facts() -> dict:
+    """Host-side limits that bound the box aggregate of the swap: memory,
+    NUMA nodes, page-locking limit and CPU model."""
+    import resource
 
-    from oracle import oracle as orc
+    facts = {"cpus": len(os.sched_getaffinity(0))}
+    try:
+        mem = {l.split(":")[0]: int(l.split()[1]) for l in open("/proc/meminfo")
+               if l.startswith(("MemTotal", "MemAvailable"))}
+        facts["mem_total_gib"] = round(mem["MemTotal"] / (1 << 20), 1)
+        facts["mem_available_gib"] = round(mem["MemAvailable"] / (1 << 20), 1)
+    except (OSError, KeyError, ValueError, IndexError):
+        pass
+    try:
+        nodes = [d for d in os.listdir("/sys/devices/system/node") if d.startswith("node")]
+        facts["numa_nodes"] = len(nodes)
+    except OSError:
+        pass
+    soft, _ = resource.getrlimit(resource.RLIMIT_MEMLOCK)
+    facts["memlock"] = "unlimited" if soft == resource.RLIM_INFINITY else soft
+    try:
+        facts["cpu"] = [l for l in open("/proc/cpuinfo")
+                        if l.startswith("model name")][0].split(":")[1].strip()
+    except (OSError, IndexError):
+        pass
+    return facts
 
-    threads = len(os.sched_getaffinity(0))
-    page = 131072
-    nsrc, ngather = 16384, 4096
-    src = np.empty(nsrc * page, np.uint8)
-    src[::4096] = 1  # touch pages
-    dst = np.empty(ngather * page, np.uint8)
+
+def host_dram_copy_gbs(nbytes: int = 4 * GIB) -> float:
+    """Host DRAM copy bandwidth on all host threads (torch's parallel CPU
+    copy between two page-locked buffers): bytes copied per second, each byte
+    read once and written once.  Best of 5 after a warm-up."""
     import torch
 
-    ids = torch.randperm(nsrc, generator=torch.Generator().manual_seed(0))[:ngather].tolist()
-    slots = list(range(ngather))
-    orc.copy_blocks_mt(ids, slots, src, dst, page, threads)  # warm
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    a = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    b = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    a.fill_(1)
+    b.copy_(a)
+    best = 0.0
+    for _ in range(5):
+        t0 = time.perf_counter()
+        b.copy_(a)
+        best = max(best, nbytes / (time.perf_counter() - t0) / 1e9)
+    del a, b
+    return best
+
+
+def cpu_baseline(seconds: float) -> dict:
+    """The reference's CPU path over the configuration-2 mapping: per K/V
+    tensor, swap-out as torch.index_select of the 1024 out-going blocks into a
+    host slot tensor and swap-in as index_copy_ of 1024 slots into the cache,
+    on all host threads.  Bounded sample: 4 of the 64 [4096,16,32,128] fp16
+    tensors (2 GiB of host cache) and the step-0 block ids, repeated for about
+    `seconds`.  The builder's threaded C gather (oracle/) is reported beside
+    it."""
+    import torch
+
+    from aegaeon_b200 import workloads
+
+    threads = len(os.sched_getaffinity(0))
+    torch.set_num_threads(threads)
+    sh = workloads.CFG2
+    n_t = 4
+    g = torch.Generator().manual_seed(0)
+    shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+    caches = [torch.empty(shape, dtype=sh.dtype).uniform_(-2.0, 2.0, generator=g)
+              for _ in range(n_t)]
+    out_ids, in_ids = workloads.swap_step_ids(sh.num_blocks, 1024, 0)
+    oi = torch.tensor(out_ids, dtype=torch.int64)
+    ii = torch.tensor(in_ids, dtype=torch.int64)
+    slots = torch.empty((1024,) + shape[1:], dtype=sh.dtype)
+    incoming = torch.empty((1024,) + shape[1:], dtype=sh.dtype).uniform_(-2.0, 2.0, generator=g)
+
+    def once():
+        for c in caches:
+            torch.index_select(c, 0, oi, out=slots)
+            c.index_copy_(0, ii, incoming)
+
+    once()  # warm
     t0 = time.perf_counter()
     reps = 0
     while True:
-        orc.copy_blocks_mt(ids, slots, src, dst, page, threads)
+        once()
         reps += 1
         if time.perf_counter() - t0 >= seconds:
             break
     dt = time.perf_counter() - t0
-    # The same gather with torch.index_select over a block-shaped host tensor,
-    # on all host threads (the CPU path named by the configuration).
+    moved = reps * n_t * 2 * 1024 * sh.page_bytes
+    # exactness of the sample: the last swap-out holds the out-going blocks
+    exact = bool(torch.equal(slots, caches[-1][oi]))
+    del caches, slots, incoming
+    port = None
+    try:
+        port = _c_port_gather(min(seconds, 5.0), threads)
+    except Exception:  # noqa: BLE001 - the side figure is optional
+        pass
+    facts = host_facts()
+    return {"value": moved / dt / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "path": "torch.index_select (swap-out) + index_copy_ (swap-in) per K/V tensor "
+                    "over the cfg2 block mapping: the reference CPU path north_star names",
+            "bit_exact": exact, "c_port_gather_gbs": port,
+            "sample": f"{reps} x (4 of 64 cfg2 tensors x [1024 out + 1024 in] x 128 KiB "
+                      f"blocks), {threads} threads, {dt:.1f} s; cpu {facts.get('cpu')}"}
+
+
+def _c_port_gather(seconds: float, threads: int) -> float:
+    """The builder's threaded C block gather (test-infrastructure oracle) on
+    the same kind of mapping: GB/s."""
+    import numpy as np
     import torch
 
-    torch.set_num_threads(threads)
-    src_t = torch.from_numpy(src).view(nsrc, page)
-    idx = torch.tensor(ids, dtype=torch.int64)
-    out_t = torch.index_select(src_t, 0, idx)
-    t1 = time.perf_counter()
-    reps_t = 0
-    while time.perf_counter() - t1 < min(seconds, 5.0):
-        torch.index_select(src_t, 0, idx, out=out_t)
-        reps_t += 1
-    torch_gbs = reps_t * ngather * page / (time.perf_counter() - t1) / 1e9
-    cpu = "unknown"
-    try:
-        cpu = [l for l in open("/proc/cpuinfo") if l.startswith("model name")][0].split(":")[1].strip()
-    except (OSError, IndexError):
-        pass
-    return {"value": reps * ngather * page / dt / 1e9, "unit": "GB/s", "cores": threads,
-            "kind": "port", "torch_index_select_gbs": torch_gbs,
-            "sample": f"{reps} x gather of {ngather} random 128 KiB blocks (512 MiB) from a "
-                      f"2 GiB host cache, {threads} threads, {dt:.1f} s; cpu {cpu}"}
+    from oracle import oracle as orc
+
+    page, nsrc, ngather = 131072, 16384, 4096
+    src = np.empty(nsrc * page, np.uint8)
+    src[::4096] = 1
+    dst = np.empty(ngather * page, np.uint8)
+    ids = torch.randperm(nsrc, generator=torch.Generator().manual_seed(0))[:ngather].tolist()
+    slots = list(range(ngather))
+    orc.copy_blocks_mt(ids, slots, src, dst, page, threads)
+    t0 = time.perf_counter()
+    reps = 0
+    while time.perf_counter() - t0 < seconds:
+        orc.copy_blocks_mt(ids, slots, src, dst, page, threads)
+        reps += 1
+    return reps * ngather * page / (time.perf_counter() - t0) / 1e9
 
 
 MIGRATION_SMALL_BLOCKS = (1, 4, 16, 64)
 
 
-def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull") -> dict:
+def _pair_exact(dist_, dev, pages, page: int, ids, is_src: bool, partner: int) -> bool:
+    """Position-keyed comparison of the moved blocks across a pair: each side
+    gathers its blocks in plan order (entry i = all segments of its i-th
+    block; torch indexing, independent of the copy path), the prefill rank
+    sends its gather over NCCL and the decode rank compares byte for byte.
+    Returns, on every rank, whether every pair matched."""
+    import torch
+    import torch.distributed as dist
+
+    idx = torch.tensor(ids, device=dev)
+    mine = torch.cat([p.view(-1, page)[idx] for p in pages], dim=1).contiguous()
+    ok = True
+    if is_src:
+        dist.send(mine, dst=partner)
+    else:
+        theirs = torch.empty_like(mine)
+        dist.recv(theirs, src=partner)
+        ok = bool(torch.equal(mine, theirs))
+        del theirs
+    del mine
+    torch.cuda.synchronize()
+    return all(x for x in dist_.gather_obj(ok))
+
+
+def _peer_copy_peak(dist_, sw, partner: int, direction: str, active: bool, stream, blocks: int,
+                    segments: int, page: int) -> dict:
+    """Copy-engine peer copy between the pair, same direction and same
+    mapped caches as the migration: blocks [0, blocks) of every segment, which
+    coalesce into one plain cudaMemcpyAsync per segment (mode ce_extent), in
+    barrier-started windows; best of 5, slowest rank."""
+    import torch
+
+    ids = list(range(blocks))
+
+    def run():
+        if active:
+            sw.migrate_blocks([0], partner, ids, ids, None, direction=direction,
+                              mode="ce_extent", stream=stream)
+
+    run()
+    stream.synchronize()
+    nbytes = blocks * segments * page
+    best = 0.0
+    for _ in range(5):
+        dist_.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        run()
+        run()
+        b.record(stream)
+        b.synchronize()
+        t = dist_.max(a.elapsed_time(b) / 1e3)
+        best = max(best, 2 * nbytes / t / 1e9)
+    return {"per_pair_gbs": best, "bytes": nbytes,
+            "how": f"one cudaMemcpyAsync per segment ({segments} x {blocks * page} B), "
+                   "issued by the active rank on the migration stream, best of 5 windows"}
+
+
+def _ipc_event_ordering(dist_, dev, sw, pages, page: int, plan, is_src: bool, partner: int,
+                        pair: int, stream) -> bool:
+    """worker.py:2351-2394 across processes: the prefill rank swaps new
+    bytes into the plan's source blocks from host rows and ships the swap's
+    interprocess event handle at once (before the swap has finished); the
+    decode rank pulls the blocks after waiting on that event.  The pulled
+    blocks must equal the swapped-in ones (position-keyed exact check)."""
+    import torch
+
+    from aegaeon_b200 import swapper
+
+    n = plan.num_blocks
+    handle = None
+    if is_src:
+        comp = len(pages) * page
+        pool = torch.empty(n * comp, dtype=torch.uint8, pin_memory=True)
+        g = torch.Generator(device=dev).manual_seed(4242 + pair)
+        fill = torch.empty(min(n * comp, GIB), dtype=torch.uint8, device=dev)
+        for o in range(0, pool.numel(), fill.numel()):
+            fill.random_(0, 256, generator=g)
+            pool[o:o + fill.numel()].copy_(fill[:pool.numel() - o])
+        del fill
+        segs, _ = swapper.make_segments([((f"l{i}",), p.numel()) for i, p in enumerate(pages)],
+                                        pages[0].numel() // page)
+        writer = swapper.KVSwapper(dev.index, segs, pages, [frozenset({0})] * len(pages), [1],
+                                   kv_swap=pool)
+        torch.cuda.synchronize()
+        dist_.barrier()
+        rows = list(range(n))
+        handle = writer.swap_blocks([pair], rows, plan.source_ids, [0] * n, [0] * n, [1] * n,
+                                    [None], True, return_handle=True)
+    else:
+        dist_.barrier()
+    handles = dist_.gather_obj(handle)
+    if not is_src:
+        sw.migrate_blocks([pair], partner, plan.source_ids, plan.target_ids, [handles[partner]],
+                          direction="pull", stream=stream)
+    torch.cuda.synchronize()
+    ok = _pair_exact(dist_, dev, pages, page, plan.source_ids if is_src else plan.target_ids,
+                     is_src, partner)
+    if is_src:
+        writer.close()
+        del pool
+    return ok
+
+
+def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull",
+                    ipc_check: bool = False) -> dict:
     """Configuration 3 at N >= 2: pairs (i, i + N/2), rank i the prefill side.
     pull: the decode rank maps the prefill rank's cache and copies the blocks
     in (loads over NVLink); push: the prefill rank stores them into the
@@ -544,9 +736,12 @@ def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull"
     plan = workloads.migration_plan(sh, requests=8, seed=0, pair=pair)
     nbytes = plan.num_blocks * sh.composite_bytes
     active = is_src if direction == "push" else not is_src
-    if active:
-        sw.register_kvcache_mem_handles(partner, None, handles[partner])
+    # both sides map the partner: the pull of the event-ordering check and the
+    # push both need it
+    sw.register_kvcache_mem_handles(partner, None, handles[partner])
     stream = torch.cuda.Stream(dev)
+    peer_peak = _peer_copy_peak(dist_, sw, partner, direction, active, stream, 2048,
+                                sh.num_segments, sh.page_bytes)
 
     def run():
         if active:
@@ -565,10 +760,11 @@ def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull"
     b.synchronize()
     t = dist_.max(a.elapsed_time(b) / 1e3)
     dist_.barrier()
+    # Exact parity of the timed migrations, position-keyed across the pair.
+    parity = _pair_exact(dist_, dev, pages, sh.page_bytes,
+                         plan.source_ids if is_src else plan.target_ids, is_src, partner)
     # Small calls: the plan's first n blocks (all 56 segments), as a decode
     # rank pulls a short request; µs per call, device time, max over ranks.
-    # The same source/target pairs as the plan, so the parity check below
-    # still holds.
     small = {}
     for n in MIGRATION_SMALL_BLOCKS:
         sub_src, sub_dst = plan.source_ids[:n], plan.target_ids[:n]
@@ -589,38 +785,44 @@ def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull"
         b.synchronize()
         small[str(n)] = dist_.max(a.elapsed_time(b) * 1e3 / 200)
         dist_.barrier()
-    # Parity of the timed push: the decode rank's blocks equal the prefill
-    # rank's (checked on a digest of the moved pages, both sides on device).
-    moved = [p.view(-1, sh.page_bytes)[plan.source_ids if is_src else plan.target_ids]
-             for p in pages]
-    digest = torch.stack([m.view(torch.int32).sum(dtype=torch.int64) for m in moved]).cpu().tolist()
-    digests = dist_.gather_obj(digest)
-    parity = all(digests[r] == digests[r + half] for r in range(half))
-    del moved
+    ipc_ok = None
+    if ipc_check:
+        ipc_ok = _ipc_event_ordering(dist_, dev, sw, pages, sh.page_bytes, plan, is_src,
+                                     partner, pair, stream)
     nccl = nccl_comparison(dist_, dev, sw, plan, is_src, partner, steps, warmup)
     sw.close()
     del pages
+    torch.cuda.empty_cache()
     total = half * nbytes * steps
     per_pair = nbytes * steps / t / 1e9
-    return {"config": "cfg3 Qwen2.5-7B P->D migration: 28 layers, 4 kv heads, 128 dim, bf16, "
-                      "block 16; 8 requests/pair, prompts U{512..8192}; pairs (i, i+N/2); "
-                      f"{direction}: " + ("decode rank loads from the prefill rank's mapped "
-                                          "cache over NVLink" if direction == "pull" else
-                                          "prefill rank stores into the decode rank's mapped "
-                                          "cache over NVLink"),
-            "pairs": half, "bytes_per_pair": nbytes, "value": total / t / 1e9, "unit": "GB/s",
-            "per_pair_gbs": per_pair, "nvlink_peer_copy_gbs": 770.0,
-            "frac_of_measured_peer_copy": per_pair / 770.0, "frac_of_nominal_900": per_pair / 900.0,
-            "ms_per_step": t / steps * 1e3, "bit_exact": parity,
-            "small_calls_us": small,
-            "small_calls_how": "per n: one migrate_blocks call moving n blocks x 56 segments "
-                               f"({sh.composite_bytes // 1024} KiB per block), 200 calls "
-                               "after 20 warm-up, CUDA events, max over ranks",
-            "nccl_sendrecv": {"value": half * nbytes / nccl / 1e9, "unit": "GB/s",
-                              "per_pair_gbs": nbytes / nccl / 1e9,
-                              "how": "gather blocks into a contiguous buffer (kvx kernel), "
-                                     "torch.distributed send/recv (NCCL), scatter on the "
-                                     "decode rank; CUDA events, max over ranks"}}
+    out = {"config": "cfg3 Qwen2.5-7B P->D migration: 28 layers, 4 kv heads, 128 dim, bf16, "
+                     "block 16; 8 requests/pair, prompts U{512..8192}; pairs (i, i+N/2); "
+                     f"{direction}: " + ("decode rank loads from the prefill rank's mapped "
+                                         "cache over NVLink" if direction == "pull" else
+                                         "prefill rank stores into the decode rank's mapped "
+                                         "cache over NVLink"),
+           "pairs": half, "bytes_per_pair": nbytes, "value": total / t / 1e9, "unit": "GB/s",
+           "per_pair_gbs": per_pair, "peer_copy_peak": peer_peak,
+           "frac_of_measured_peer_copy": per_pair / peer_peak["per_pair_gbs"],
+           "frac_of_nominal_900": per_pair / 900.0,
+           "ms_per_step": t / steps * 1e3, "bit_exact": parity,
+           "bit_exact_how": "every moved block, all 56 segments, compared byte for byte across "
+                            "the pair in plan order (prefill gather sent over NCCL)",
+           "small_calls_us": small,
+           "small_calls_how": "per n: one migrate_blocks call moving n blocks x 56 segments "
+                              f"({sh.composite_bytes // 1024} KiB per block), 200 calls "
+                              "after 20 warm-up, CUDA events, max over ranks",
+           "nccl_sendrecv": {"value": half * nbytes / nccl / 1e9, "unit": "GB/s",
+                             "per_pair_gbs": nbytes / nccl / 1e9,
+                             "how": "gather blocks into a contiguous buffer (kvx kernel), "
+                                    "torch.distributed send/recv (NCCL), scatter on the "
+                                    "decode rank; CUDA events, max over ranks"}}
+    if ipc_check:
+        out["ipc_event_ordering"] = ipc_ok
+        out["ipc_event_ordering_how"] = (
+            "prefill swaps new bytes into the source blocks and ships the swap's IPC event "
+            "handle before it completes; decode pulls after waiting on it; exact check")
+    return out
 
 
 def nccl_comparison(dist_, dev, sw, plan, is_src, partner, steps, warmup) -> float:
@@ -683,6 +885,40 @@ def traffic_from_profile() -> float | None:
 
 
 # ---- arms --------------------------------------------------------------------------
+def blocks_per_direction(requested: int, world: int, cache_blocks: int) -> int:
+    """Blocks each way per step: `requested`, unless 2 x that many 8 MiB
+    page-locked host rows per rank would not fit in 45% of the host's
+    available memory (then fewer, a multiple of 16; stated in the config)."""
+    from aegaeon_b200 import workloads
+
+    per_dir = requested
+    try:
+        avail = int([l for l in open("/proc/meminfo")
+                     if l.startswith("MemAvailable")][0].split()[1]) * 1024
+        rows_fit = int(0.45 * avail / world / workloads.CFG2.composite_bytes)
+        if 2 * per_dir > rows_fit:
+            per_dir = max(64, rows_fit // 2 // 16 * 16)
+    except (OSError, IndexError, ValueError):
+        pass
+    return min(per_dir, cache_blocks // 2)
+
+
+def cfg2_config(per_dir: int, cache_blocks: int, world: int) -> dict:
+    """The `config` object of both arms (identical, so the lines compare)."""
+    from aegaeon_b200 import workloads
+
+    return {
+        "workload": "cfg2 Llama-2-7B-shaped per-GPU swap: 32 layers x separate K/V "
+                    f"[{cache_blocks},16,32,128] fp16 U(-2,2) seed 0; per step {per_dir} "
+                    f"random blocks out to host and {per_dir} other random blocks in from "
+                    "host, out and in on two streams concurrently; every GPU independent",
+        "blocks_per_direction": per_dir,
+        "bytes_per_step_per_gpu": 2 * per_dir * workloads.CFG2.composite_bytes,
+        "l2": "no flush needed: 8 GiB per direction per step, far larger than the 126 MB L2",
+        "parallelism": f"independent swap per GPU x{world}",
+    }
+
+
 def run_kvx(args):
     import torch
 
@@ -690,18 +926,12 @@ def run_kvx(args):
 
     dist_ = Dist.init(use_pg=True)
     dev = torch.device("cuda", dist_.local_rank)
-    per_dir = args.blocks
-    # Host RAM guard: 2 * per_dir rows of 8 MiB page-locked per rank.
-    try:
-        avail = int([l for l in open("/proc/meminfo") if l.startswith("MemAvailable")][0].split()[1]) * 1024
-        rows_fit = int(0.45 * avail / dist_.world / workloads.CFG2.composite_bytes)
-        if 2 * per_dir > rows_fit:
-            per_dir = max(64, rows_fit // 2 // 16 * 16)
-    except (OSError, IndexError, ValueError):
-        pass
+    per_dir = blocks_per_direction(args.blocks, dist_.world, args.cache_blocks)
     peaks = host_link_peaks(dev, dist_)  # all ranks at once: the box's concurrent peak
     box_peak = peaks["box_bidir_gbs"]
-    per_dir = min(per_dir, args.cache_blocks // 2)
+    # host DRAM copy bandwidth: a property of the box, measured by rank 0 alone
+    dram = host_dram_copy_gbs() if dist_.rank == 0 else None
+    dist_.barrier()
     bench = SwapBench(dev, per_dir, args.cache_blocks)
     lists = [bench.step_lists(k) for k in range(args.warmup + args.steps)]
     for k in range(args.warmup):
@@ -732,13 +962,21 @@ def run_kvx(args):
     bytes_total = bench.bytes_per_step * args.steps * dist_.world
     value = bytes_total / t_dev / 1e9
     e2e = bytes_total / t_e2e / 1e9
+    extras = None
+    if dist_.world == 1 and not args.no_extras:
+        extras = baseline_configs(dev, bench)
     bench.close()
     del bench
     torch.cuda.empty_cache()
-    mig = None
+    mig = mig_push = None
     if dist_.world >= 2 and not args.no_migration:
         mig = migration_bench(dist_, dev, steps=args.steps, warmup=args.warmup,
-                              direction=args.migration_direction)
+                              direction="pull", ipc_check=True)
+        mig_push = migration_bench(dist_, dev, steps=args.steps, warmup=args.warmup,
+                                   direction="push")
+    cpu = None
+    if dist_.rank == 0 and dist_.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(args.cpu_seconds)
     mp = measured_peaks()
     hbm_peak = mp.get("hbm_gbs", 6650.0)
     per_gpu = value / dist_.world
@@ -748,6 +986,17 @@ def run_kvx(args):
         achieved_k = k_bytes / (k_ms / 1e3) / 1e9 if k_ms > 0 else None
         traffic = traffic_from_profile()
         k_name = ("kvx_copy_bulk<GridList>" if mode_used == "ce" else "kvx_copy_vec<GridList>")
+        facts = host_facts()
+        host_link = {
+            "bound": "host_link", "achieved_box_gbs": value, "box_peak_gbs": box_peak,
+            "frac": value / box_peak, "per_gpu_gbs": per_gpu,
+            "per_gpu_peak_h2d_gbs": peaks["h2d_gbs"], "per_gpu_peak_d2h_gbs": peaks["d2h_gbs"],
+            "host_dram_copy_gbs": dram,
+            "host": {k: facts.get(k) for k in ("cpus", "numa_nodes", "mem_total_gib", "memlock")},
+            "limiter": ("PCIe link of the one GPU" if dist_.world == 1 else
+                        "host memory shared by all GPUs' copy engines: every payload byte is "
+                        "written to (swap-out) or read from (swap-in) host DRAM"),
+        }
         line = {
             "metric": METRIC,
             "value": value,
@@ -762,21 +1011,9 @@ def run_kvx(args):
             "dtype": "u8",
             "data": "synthetic: fp16 U(-2,2) from seed 0, block ids from seeded randperm "
                     "(no real checkpoint or trace)",
-            "config": {
-                "workload": "cfg2 Llama-2-7B-shaped per-GPU swap: 32 layers x separate K/V "
-                            f"[{args.cache_blocks},16,32,128] fp16; per step "
-                            f"{per_dir} random blocks out (host rows 0..{per_dir - 1}) and "
-                            f"{per_dir} other random blocks in, on the swap-out / swap-in "
-                            "streams concurrently",
-                "blocks_per_direction": per_dir,
-                "bytes_per_step_per_gpu": bench_bytes(per_dir),
-                "api": "KVSwapper.swap_blocks (Worker.swap_blocks replacement) -> "
-                       "kvx_swap_blocks",
-                "transfer_mode": f"{args.mode} -> {mode_used}",
-                "l2": "no flush needed: 8 GiB per direction per step, far larger than the "
-                      "126 MB L2",
-                "parallelism": f"independent swap per GPU x{dist_.world}",
-            },
+            "config": cfg2_config(per_dir, args.cache_blocks, dist_.world),
+            "api": "KVSwapper.swap_blocks (Worker.swap_blocks replacement) -> kvx_swap_blocks; "
+                   f"transfer mode {args.mode} -> {mode_used}",
             "roofline": {
                 "bound": "hbm",
                 "kernel": k_name,
@@ -785,6 +1022,7 @@ def run_kvx(args):
                 "unit": "GB/s",
                 "frac": (achieved_k / hbm_peak) if achieved_k else None,
                 "traffic": traffic,
+                "host_link": host_link,
                 "peak_source": "MEASURED_PEAKS.json hbm_gbs (burst copy, read+write), of measured"
                                if "hbm_gbs" in mp else "fallback 6650 GB/s, of fallback",
                 "how": "live: CUDA events around every launch of the copy kernel on its stream "
@@ -823,7 +1061,7 @@ def run_kvx(args):
                 "peak_h2d_gbs": peaks["h2d_gbs"],
                 "peak_d2h_gbs": peaks["d2h_gbs"],
                 "nominal_gbs_per_direction": 63.0,
-                "note": "the binding roofline of the swap: payload crosses PCIe Gen5 x16",
+                "host": facts,
             },
             "e2e": {
                 "value": e2e,
@@ -834,27 +1072,38 @@ def run_kvx(args):
                 "seconds": t_e2e,
             },
             "gpu_launches": launches,
-            "clocks": clk,
         }
         if mig is not None:
             line["migration"] = mig
-    if dist_.rank == 0 and dist_.world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+            line["migration_push"] = mig_push
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        line["clocks"] = clk
+        # Compact summaries last: they stay in the tail of the line.
+        line["host_link"] = {k: (round(v, 3) if isinstance(v, float) else v)
+                             for k, v in host_link.items() if k not in ("host", "limiter")}
+        if mig is not None:
+            line["migration_summary"] = {
+                d: {"per_pair_gbs": round(m["per_pair_gbs"], 1),
+                    "frac_of_900": round(m["frac_of_nominal_900"], 3),
+                    "peer_copy_gbs": round(m["peer_copy_peak"]["per_pair_gbs"], 1),
+                    "frac_of_peer_copy": round(m["frac_of_measured_peer_copy"], 3),
+                    "bit_exact": m["bit_exact"], "ipc_event_ordering": m.get("ipc_event_ordering")}
+                for d, m in (("pull", mig), ("push", mig_push))}
+        if extras is not None:
+            line["baseline_configs"] = extras
     dist_.finish()
     if line is not None:
         emit(line)
 
 
-def bench_bytes(per_dir: int) -> int:
-    from aegaeon_b200 import workloads
-
-    return 2 * per_dir * workloads.CFG2.composite_bytes
-
-
 def run_reference(args):
-    rank = int(os.environ.get("RANK", "0"))
-    if rank != 0:
-        return
+    """The reference's own swap op (ops/swap.cu, built unmodified from the
+    reference sources into oracle/_ref) on configuration 2: one call per K/V
+    tensor, one cudaMemcpyAsync per block, out and in on two streams, issued
+    from one host thread per GPU.  At N > 1 every rank swaps its own cache, as
+    one reference Worker per GPU does (aegaeon/llm.py:992-1017); the box
+    aggregate uses the slowest rank's time."""
     import torch
 
     from aegaeon_b200 import workloads
@@ -864,31 +1113,34 @@ def run_reference(args):
 
         ref = build_ref.load_module()
     except Exception as e:  # noqa: BLE001
-        emit({"impl": "reference", "unavailable": f"reference op not built: {e}"})
+        if int(os.environ.get("RANK", "0")) == 0:
+            emit({"impl": "reference", "unavailable": f"reference op not built: {e}"})
         return
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
+    dist_ = Dist.init(use_pg=True)
+    dev = torch.device("cuda", dist_.local_rank)
     sh = workloads.CFG2
-    per_dir = args.blocks
+    per_dir = blocks_per_direction(args.blocks, dist_.world, args.cache_blocks)
+    nb = args.cache_blocks
     gen = torch.Generator(device=dev).manual_seed(0)
     caches = []
     for _ in range(sh.num_segments):
-        t = torch.empty((sh.num_blocks, 16, sh.kv_heads, sh.head_dim), dtype=sh.dtype, device=dev)
+        t = torch.empty((nb, 16, sh.kv_heads, sh.head_dim), dtype=sh.dtype, device=dev)
         t.uniform_(-2.0, 2.0, generator=gen)
         caches.append(t)
-    out_host = [torch.empty((per_dir, 16, sh.kv_heads, sh.head_dim), dtype=sh.dtype).pin_memory()
-                for _ in range(sh.num_segments)]
-    in_host = [torch.empty_like(h).pin_memory() for h in out_host]
+    out_host = [torch.empty((per_dir, 16, sh.kv_heads, sh.head_dim), dtype=sh.dtype,
+                            pin_memory=True) for _ in range(sh.num_segments)]
+    in_host = [torch.empty_like(h, pin_memory=True) for h in out_host]
     s_out, s_in = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     slots = list(range(per_dir))
     live = args.ref_variant == "live-loop"
     if live:
         # composite host rows: row r holds every segment's page of one block
         page = sh.page_bytes
-        pool_out = torch.empty((per_dir, sh.num_segments * page), dtype=torch.uint8).pin_memory()
-        pool_in = torch.empty((per_dir, sh.num_segments * page), dtype=torch.uint8).pin_memory()
-        gpu_pages = [c.view(torch.uint8).view(sh.num_blocks, page) for c in caches]
+        pool_out = torch.empty((per_dir, sh.num_segments * page), dtype=torch.uint8,
+                               pin_memory=True)
+        pool_in = torch.empty((per_dir, sh.num_segments * page), dtype=torch.uint8,
+                              pin_memory=True)
+        gpu_pages = [c.view(torch.uint8).view(nb, page) for c in caches]
 
     def live_loop(pool, ids, is_swap_in):
         # worker.py:2272-2329 restated: per segment, per entry, one copy_
@@ -902,7 +1154,7 @@ def run_reference(args):
                     cpu_page.copy_(pages[blk].narrow(0, 0, page), non_blocking=True)
 
     def step(k):
-        out_ids, in_ids = workloads.swap_step_ids(sh.num_blocks, per_dir, k)
+        out_ids, in_ids = workloads.swap_step_ids(nb, per_dir, k)
         with torch.cuda.stream(s_out):
             if live:
                 live_loop(pool_out, out_ids, False)
@@ -925,6 +1177,7 @@ def run_reference(args):
         step(k)
     torch.cuda.synchronize()
     clocks = ClockSampler(gpu_uuid(dev))
+    dist_.barrier()
     clocks.start()
     cur = torch.cuda.current_stream(dev)
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -940,15 +1193,26 @@ def run_reference(args):
     b.synchronize()
     wall = time.perf_counter() - t0
     clk = clocks.stop()
-    t = a.elapsed_time(b) / 1e3
-    nbytes = 2 * per_dir * sh.composite_bytes * args.steps
+    t = dist_.max(a.elapsed_time(b) / 1e3)
+    wall = dist_.max(wall)
+    # the last step's swap-out must hold its blocks (checked on every rank)
+    last_out, _ = workloads.swap_step_ids(nb, per_dir, args.warmup + args.steps - 1)
+    oi = torch.tensor(last_out, device=dev)
+    exact = all(torch.equal(h.to(dev).view(torch.uint8), c[oi].view(torch.uint8))
+                for c, h in zip(caches[:4], out_host[:4])) if not live else None
+    exact_all = dist_.gather_obj(exact)
+    dist_.finish()
+    if dist_.rank != 0:
+        return
+    per_step = per_dir * sh.composite_bytes * dist_.world
+    nbytes = 2 * per_step * args.steps
     value = nbytes / t / 1e9
-    line = {
+    emit({
         "impl": "reference",
         "metric": METRIC,
         "value": value,
         "unit": "GB/s",
-        "n_gpus": 1,
+        "n_gpus": dist_.world,
         "steps": args.steps,
         "warmup": args.warmup,
         "ms_per_step": t / args.steps * 1e3,
@@ -956,28 +1220,26 @@ def run_reference(args):
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "u8",
-        "data": "synthetic: fp16 U(-2,2) from seed 0, block ids from seeded randperm",
-        "config": {
-            "workload": "cfg2 Llama-2-7B-shaped per-GPU swap: 32 layers x separate K/V "
-                        f"[4096,16,32,128] fp16; per step {per_dir} random blocks out and "
-                        f"{per_dir} in, out and in on two streams",
-            "blocks_per_direction": per_dir,
-            "api": ("restated Worker.swap_blocks hot loop (worker.py:2270-2329): one torch "
-                    "copy_(non_blocking=True) per segment and block into composite host rows"
-                    if live else
-                    "reference aegaeon.ops.swap (ops/swap.cu, built unmodified from the "
-                    "reference sources): one call per K/V tensor, one cudaMemcpyAsync per block"),
-            "l2": "no flush needed: 8 GiB per direction per step",
-        },
-        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": 1, "kind": "reference",
-                         "sample": f"full workload, {args.steps} steps; one host thread issues "
-                                   f"{2 * per_dir * sh.num_segments} copies per step"},
-        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0,
-                "d2h_bytes_per_step": 0, "wall_clock_gbs": nbytes / wall / 1e9},
+        "data": "synthetic: fp16 U(-2,2) from seed 0, block ids from seeded randperm "
+                "(no real checkpoint or trace)",
+        "config": cfg2_config(per_dir, nb, dist_.world),
+        "api": ("restated Worker.swap_blocks hot loop (worker.py:2270-2329): one torch "
+                "copy_(non_blocking=True) per segment and block into composite host rows"
+                if live else
+                "reference aegaeon.ops.swap (ops/swap.cu, built unmodified from the reference "
+                "sources): one call per K/V tensor, one cudaMemcpyAsync per block"),
+        "bit_exact_last_swap_out": exact_all if not live else None,
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": dist_.world,
+                         "kind": "reference",
+                         "sample": f"full workload, {args.steps} steps; one host thread per GPU "
+                                   f"issues {2 * per_dir * sh.num_segments} copies per step"},
+        "e2e": {"value": nbytes / wall / 1e9, "unit": "GB/s", "h2d_bytes_per_step": per_step,
+                "d2h_bytes_per_step": per_step,
+                "how": "the op takes host buffers: every payload byte crosses the host link "
+                       "inside the timed region; wall clock, slowest rank"},
         "gpu_launches": 0,
         "clocks": clk,
-    }
-    emit(line)
+    })
 
 
 # ---- configurations 1, 4 and 5 (one JSON line each, N=1 unless stated) ---------
@@ -1005,225 +1267,453 @@ def _timed(stream_list, fn, steps, dev):
     return a.elapsed_time(b) / 1e3
 
 
-def run_config1(args):
-    """Qwen3-4B round trip through the per-tensor op: 72 tensors [1024,16,8,128]
-    bf16 N(0,1); 256 blocks out to slots 0..255, then back in to a fresh
-    permutation of a zeroed cache; bit-exact check of the round trip."""
+def _bytes_equal_chunked(dev, host_u8, device_u8_fn, rows: int, row_bytes: int,
+                         chunk_rows: int) -> bool:
+    """host_u8 (page-locked, rows x row_bytes) equals device_u8_fn(r0, r1)
+    (a (r1-r0) x row_bytes uint8 device tensor) for every chunk of rows;
+    compared on the device."""
     import torch
 
-    from aegaeon_b200 import ops, workloads
+    for r0 in range(0, rows, chunk_rows):
+        r1 = min(rows, r0 + chunk_rows)
+        h = host_u8[r0 * row_bytes:r1 * row_bytes].to(dev, non_blocking=False)
+        if not torch.equal(h.view(r1 - r0, row_bytes), device_u8_fn(r0, r1)):
+            return False
+    return True
+
+
+class Cfg1:
+    """Configuration 1 (Qwen3-4B round trip) through the per-tensor op: 72
+    tensors [1024,16,8,128] bf16 N(0,1) from seed 0; 256 blocks out to slots
+    0..255, then back in to a fresh permutation of a zeroed cache.  Either
+    arm: this build's ops.swap or the reference's compiled op."""
+
+    N = 256
+
+    def __init__(self, dev):
+        import torch
+
+        from aegaeon_b200 import workloads
+
+        self.dev = dev
+        self.sh = sh = workloads.CFG1
+        gen = torch.Generator(device=dev).manual_seed(0)
+        self.shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+        self.caches = [torch.empty(self.shape, dtype=sh.dtype, device=dev).normal_(generator=gen)
+                       for _ in range(sh.num_segments)]
+        self.back = [torch.zeros_like(c) for c in self.caches]
+        self.hosts = [torch.empty((self.N,) + self.shape[1:], dtype=sh.dtype, pin_memory=True)
+                      for _ in self.caches]
+        self.out_ids = workloads.randperm(sh.num_blocks, 0)[:self.N]
+        self.in_ids = workloads.randperm(sh.num_blocks, 1)[:self.N]
+        self.slots = list(range(self.N))
+        self.step_bytes = 2 * sh.num_segments * self.N * sh.page_bytes
+
+    def run(self, impl: str, steps: int, warmup: int, mode: str = "auto", ref=None) -> dict:
+        import torch
+
+        from aegaeon_b200 import ops
+
+        for b in self.back:
+            b.zero_()
+        for h in self.hosts:
+            h.zero_()
+
+        def swap(src, dst, is_in, cache, host):
+            if impl == "reference":
+                ref.swap(src, dst, is_in, cache, host)
+            else:
+                ops.swap(src, dst, is_in, cache, host, mode=mode)
+
+        def step(_k):
+            for c, h in zip(self.caches, self.hosts):
+                swap(self.out_ids, self.slots, False, c, h)
+            for c, h in zip(self.back, self.hosts):
+                swap(self.slots, self.in_ids, True, c, h)
+
+        for k in range(warmup):
+            step(k)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        t = _timed([], step, steps, self.dev)
+        wall = time.perf_counter() - t0
+        oi = torch.tensor(self.out_ids, device=self.dev)
+        ii = torch.tensor(self.in_ids, device=self.dev)
+        exact = all(torch.equal(b[ii].view(torch.uint8), c[oi].view(torch.uint8)) and
+                    torch.equal(h.to(self.dev).view(torch.uint8), c[oi].view(torch.uint8))
+                    for b, c, h in zip(self.back, self.caches, self.hosts))
+        return {"seconds": t, "wall": wall, "gbs": self.step_bytes * steps / t / 1e9,
+                "e2e_gbs": self.step_bytes * steps / wall / 1e9, "bit_exact": bool(exact)}
+
+    def close(self):
+        del self.caches, self.back, self.hosts
+
+
+class Cfg4:
+    """Configuration 4 (model-switch overlap): swap-in of 2048 cfg2 blocks
+    (16 GiB) while a Qwen1.5-14B TP-2 weight shard (14.17 GB bf16, four
+    safetensors-sized storages) is uploaded from page-locked host memory on a
+    second stream.  The cfg2 cache (64 segments) and its 2048-row host pool
+    are reused from the headline run when given.
+
+    kvx arm: switch_in (KV swap-in through kvx_swap_blocks, weights through
+    kvx_upload_weights in 64 MiB chunks).  Reference arm: the reference op per
+    K/V tensor for the KV (host slots carved from the same pool, one
+    contiguous region per tensor) and one copy_(non_blocking=True) per weight
+    storage (quick_loader.py:340)."""
+
+    N = 2048
+    FILES = 4
+
+    def __init__(self, dev, pages=None, pool=None, segments=None):
+        import torch
+
+        from aegaeon_b200 import swapper, workloads
+
+        self.dev = dev
+        self.sh = sh = workloads.CFG2
+        if pages is None:
+            gen = torch.Generator(device=dev).manual_seed(0)
+            pages = []
+            for _ in range(sh.num_segments):
+                t = torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
+                workloads.fill_segment(t, sh, gen)
+                pages.append(t)
+            segments, _ = swapper.make_segments(
+                [((f"l{i}",), sh.num_blocks * sh.page_bytes) for i in range(sh.num_segments)],
+                sh.num_blocks)
+            pool = torch.empty(self.N * sh.composite_bytes, dtype=torch.uint8, pin_memory=True)
+            fill = torch.empty(GIB, dtype=torch.uint8, device=dev).random_(0, 256, generator=gen)
+            for o in range(0, pool.numel(), fill.numel()):
+                pool[o:o + fill.numel()].copy_(fill[:pool.numel() - o])
+            del fill
+        self.pages, self.pool, self.segments = pages, pool, segments
+        self.ws = workloads.WeightShard()
+        gen = torch.Generator(device=dev).manual_seed(4)
+        self.w_dev = torch.empty(self.ws.nbytes, dtype=torch.uint8, device=dev)
+        self.w_host = torch.empty(self.ws.nbytes, dtype=torch.uint8, pin_memory=True)
+        fill = torch.empty(GIB, dtype=torch.uint8, device=dev).random_(0, 256, generator=gen)
+        for o in range(0, self.ws.nbytes, fill.numel()):
+            self.w_host[o:o + fill.numel()].copy_(fill[:self.ws.nbytes - o])
+        del fill
+        self.in_ids = workloads.randperm(sh.num_blocks, 7)[:self.N]
+        self.kv_bytes = self.N * sh.composite_bytes
+        self.s_kv, self.s_w = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        # storages of the reference arm: the shard cut into FILES pieces
+        cut = -(-self.ws.nbytes // self.FILES)
+        self.files = [(o, min(self.ws.nbytes, o + cut)) for o in range(0, self.ws.nbytes, cut)]
+
+    def _check(self, impl) -> bool:
+        import torch
+
+        sh, page = self.sh, self.sh.page_bytes
+        ii = torch.tensor(self.in_ids, device=self.dev)
+        if impl == "reference":
+            # tensor s's host slots are the contiguous region s of the pool
+            for s, p in enumerate(self.pages):
+                region = self.pool[s * self.N * page:(s + 1) * self.N * page]
+                cache = p.view(-1, page)
+                if not _bytes_equal_chunked(self.dev, region, lambda r0, r1: cache[ii[r0:r1]],
+                                            self.N, page, 1024):
+                    return False
+        else:
+            comp = sh.composite_bytes
+
+            def gathered(r0, r1):
+                return torch.cat([p.view(-1, page)[ii[r0:r1]] for p in self.pages], dim=1)
+
+            if not _bytes_equal_chunked(self.dev, self.pool, gathered, self.N, comp, 128):
+                return False
+        return _bytes_equal_chunked(self.dev, self.w_host, lambda r0, r1: self.w_dev[
+            r0 * GIB:r1 * GIB].view(r1 - r0, GIB), self.ws.nbytes // GIB, GIB, 1) and \
+            torch.equal(self.w_dev[self.ws.nbytes // GIB * GIB:],
+                        self.w_host[self.ws.nbytes // GIB * GIB:].to(self.dev))
+
+    def run(self, impl: str, steps: int, warmup: int, mode: str = "auto", ref=None,
+            sw=None) -> dict:
+        import torch
+
+        from aegaeon_b200 import swapper, switch
+
+        sh, n = self.sh, self.N
+        self.w_dev.zero_()
+        if impl == "reference":
+            page = sh.page_bytes
+            shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+            caches = [p.view(sh.dtype).view(shape) for p in self.pages]
+            hosts = [self.pool[s * n * page:(s + 1) * n * page].view(sh.dtype).view(
+                (n,) + shape[1:]) for s in range(sh.num_segments)]
+            slots = list(range(n))
+
+            def step(_k):
+                with torch.cuda.stream(self.s_kv):
+                    for c, h in zip(caches, hosts):
+                        ref.swap(slots, self.in_ids, True, c, h)
+                with torch.cuda.stream(self.s_w):
+                    for a, b in self.files:
+                        self.w_dev[a:b].copy_(self.w_host[a:b], non_blocking=True)
+        else:
+            own = sw is None
+            if own:
+                sw = swapper.KVSwapper(self.dev.index, self.segments, self.pages,
+                                       [frozenset({0})] * sh.num_segments, [1], kv_swap=self.pool)
+            rows = list(range(n))
+            z, one = [0] * n, [1] * n
+
+            def step(_k):
+                switch.switch_in(sw, [(self.w_dev, self.w_host)], [0], rows, self.in_ids, z, z,
+                                 one, [None], chunk_bytes=64 << 20, kv_stream=self.s_kv,
+                                 weight_stream=self.s_w, mode=mode)
+
+        for k in range(warmup):
+            step(k)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        t = _timed([self.s_kv, self.s_w], step, steps, self.dev)
+        wall = time.perf_counter() - t0
+        exact = self._check(impl)
+        if impl != "reference" and own:
+            sw.close()
+        per = t / steps
+        return {"seconds": t, "wall": wall, "switch_ms": per * 1e3,
+                "gbs": (self.kv_bytes + self.ws.nbytes) / per / 1e9,
+                "e2e_gbs": (self.kv_bytes + self.ws.nbytes) * steps / wall / 1e9,
+                "bit_exact": bool(exact)}
+
+    def close(self):
+        del self.w_dev, self.w_host, self.pages, self.pool
+
+
+class Cfg5:
+    """Configuration 5 (fragmented swap-out): Qwen1.5-MoE-A2.7B pages (16 kv
+    heads x 128 dim bf16, 64 KiB per K or V page), a 16,384-entry mapping with
+    half the entries in contiguous device runs of 1..32 blocks and half
+    isolated; host slots sequential; one call per step.  `layers` may be
+    below 24 to bound the host memory and time of a run (stated in the
+    output)."""
+
+    def __init__(self, dev, layers: int = 24, entries: int = 16384, seed: int = 0):
+        import dataclasses
+
+        import torch
+
+        from aegaeon_b200 import swapper, workloads
+
+        self.dev = dev
+        self.sh = sh = dataclasses.replace(workloads.CFG5, layers=layers)
+        self.n = entries
+        self.ids, self.slots = workloads.fragmented_mapping(entries, sh.num_blocks, seed=seed)
+        gen = torch.Generator(device=dev).manual_seed(seed)
+        self.pages = []
+        for _ in range(sh.num_segments):
+            t = torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
+            workloads.fill_segment(t, sh, gen)
+            self.pages.append(t)
+        self.segments, self.comp = swapper.make_segments(
+            [((f"l{i}",), sh.num_blocks * sh.page_bytes) for i in range(sh.num_segments)],
+            sh.num_blocks)
+        self.pool = torch.empty(entries * self.comp, dtype=torch.uint8, pin_memory=True)
+        self.s = torch.cuda.Stream(dev)
+        self.call_bytes = entries * self.comp
+
+    def _check(self, impl) -> bool:
+        import torch
+
+        page, n = self.sh.page_bytes, self.n
+        idx = torch.tensor(self.ids, device=self.dev)
+        if impl == "reference":
+            for s, p in enumerate(self.pages):
+                region = self.pool[s * n * page:(s + 1) * n * page]
+                cache = p.view(-1, page)
+                if not _bytes_equal_chunked(self.dev, region, lambda r0, r1: cache[idx[r0:r1]],
+                                            n, page, 4096):
+                    return False
+            return True
+
+        def gathered(r0, r1):
+            return torch.cat([p.view(-1, page)[idx[r0:r1]] for p in self.pages], dim=1)
+
+        return _bytes_equal_chunked(self.dev, self.pool, gathered, n, self.comp,
+                                    max(1, GIB // self.comp))
+
+    def run(self, impl: str, steps: int, warmup: int, mode: str = "auto", ref=None) -> dict:
+        import torch
+
+        from aegaeon_b200 import swapper
+
+        sh, n = self.sh, self.n
+        self.pool.zero_()
+        if impl == "reference":
+            page = sh.page_bytes
+            shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
+            caches = [p.view(sh.dtype).view(shape) for p in self.pages]
+            hosts = [self.pool[s * n * page:(s + 1) * n * page].view(sh.dtype).view(
+                (n,) + shape[1:]) for s in range(sh.num_segments)]
+
+            def step(_k):
+                with torch.cuda.stream(self.s):
+                    for c, h in zip(caches, hosts):
+                        ref.swap(self.ids, self.slots, False, c, h)
+        else:
+            sw = swapper.KVSwapper(self.dev.index, self.segments, self.pages,
+                                   [frozenset({0})] * sh.num_segments, [1], kv_swap=self.pool)
+            z, one = [0] * n, [1] * n
+
+            def step(_k):
+                sw.swap_blocks([0], self.ids, self.slots, z, z, one, [None], False, mode=mode,
+                               stream=self.s)
+
+        for k in range(warmup):
+            step(k)
+        torch.cuda.synchronize()
+        lat = []
+        t0 = time.perf_counter()
+        for k in range(steps):
+            lat.append(_timed([self.s], step, 1, self.dev))
+        wall = time.perf_counter() - t0
+        exact = self._check(impl)
+        if impl != "reference":
+            sw.close()
+        t = sum(lat)
+        return {"seconds": t, "wall": wall, "gbs": self.call_bytes * steps / t / 1e9,
+                "e2e_gbs": self.call_bytes * steps / wall / 1e9,
+                "call_ms": sorted(x * 1e3 for x in lat), "bit_exact": bool(exact)}
+
+    def close(self):
+        del self.pages, self.pool
+
+
+def _ref_or_none():
+    try:
+        return _ref_module()
+    except Exception:  # noqa: BLE001 - reported as a missing arm
+        return None
+
+
+def baseline_configs(dev, bench, cfg5_layers: int = 4) -> dict:
+    """Configurations 1, 4 and 5 of BASELINE.json, both arms in this
+    process, for the default N=1 line: a few timed steps each, every arm's
+    output checked byte for byte afterwards."""
+    import torch
+
+    from aegaeon_b200 import workloads
+
+    ref = _ref_or_none()
+    out = {}
+
+    def pair(name, obj, steps, warmup, extra=None, **kw):
+        k = obj.run("kvx", steps, warmup, **kw)
+        r = obj.run("reference", steps, warmup, ref=ref) if ref is not None else None
+        rec = {"kvx_gbs": round(k["gbs"], 2),
+               "reference_gbs": round(r["gbs"], 2) if r else None,
+               "ratio": round(k["gbs"] / r["gbs"], 2) if r else None,
+               "bit_exact": k["bit_exact"] and (r["bit_exact"] if r else True),
+               "steps": steps}
+        if extra:
+            rec.update(extra(k, r))
+        out[name] = rec
+
+    c1 = Cfg1(dev)
+    pair("cfg1", c1, 5, 2)
+    c1.close()
+    del c1
+    torch.cuda.empty_cache()
+    reuse = bench.rows >= Cfg4.N and bench.shape.num_blocks == workloads.CFG2.num_blocks
+    c4 = Cfg4(dev, bench.pages, bench.pool, bench.segments) if reuse else Cfg4(dev)
+    pair("cfg4", c4, 3, 1, extra=lambda k, r: {
+        "kvx_switch_ms": round(k["switch_ms"], 1),
+        "reference_switch_ms": round(r["switch_ms"], 1) if r else None},
+        sw=bench.sw if reuse else None)
+    c4.close()
+    del c4
+    torch.cuda.empty_cache()
+    c5 = Cfg5(dev, layers=cfg5_layers)
+    pair("cfg5", c5, 3, 1, extra=lambda k, r: {
+        "layers": cfg5_layers, "kvx_call_ms": round(statistics.median(k["call_ms"]), 1),
+        "reference_call_ms": round(statistics.median(r["call_ms"]), 1) if r else None})
+    c5.close()
+    del c5
+    torch.cuda.empty_cache()
+    out["how"] = ("both arms here, same inputs; cfg1 72 tensors x 256 blocks out+in; cfg4 "
+                  "2048-block swap-in + 14.17 GB weights; cfg5 16384 fragmented entries, "
+                  f"{cfg5_layers} of 24 layers; outputs compared byte for byte")
+    return out
+
+
+def _line_for(args, r: dict, workload: str, impl: str, extra: dict = None) -> dict:
+    line = {"impl": impl, "metric": METRIC, "value": r["gbs"], "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": r["seconds"] / args.steps * 1e3, "higher_is_better": True,
+            "dtype": "u8", "data": "synthetic, seeded", "config": {"workload": workload},
+            "bit_exact": r["bit_exact"],
+            "e2e": {"value": r["e2e_gbs"], "unit": "GB/s"}}
+    line.update(extra or {})
+    return line
+
+
+def run_config1(args):
+    import torch
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    sh = workloads.CFG1
-    gen = torch.Generator(device=dev).manual_seed(0)
-    shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
-    caches = [torch.empty(shape, dtype=sh.dtype, device=dev).normal_(generator=gen)
-              for _ in range(sh.num_segments)]
-    back = [torch.zeros_like(c) for c in caches]
-    n = 256
-    hosts = [torch.empty((n,) + shape[1:], dtype=sh.dtype).pin_memory() for _ in caches]
-    out_ids = workloads.randperm(sh.num_blocks, 0)[:n]
-    in_ids = workloads.randperm(sh.num_blocks, 1)[:n]
-    slots = list(range(n))
-    ref = _ref_module() if args.impl == "reference" else None
-
-    def swap(src, dst, is_in, cache, host):
-        if ref is not None:
-            ref.swap(src, dst, is_in, cache, host)
-        else:
-            ops.swap(src, dst, is_in, cache, host, mode=args.mode)
-
-    def step(_k):
-        for c, h in zip(caches, hosts):
-            swap(out_ids, slots, False, c, h)
-        for c, h in zip(back, hosts):
-            swap(slots, in_ids, True, c, h)
-
-    for k in range(args.warmup):
-        step(k)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    t = _timed([], step, args.steps, dev)
-    wall = time.perf_counter() - t0
-    exact = all(torch.equal(b[in_ids].view(torch.uint8), c[out_ids].view(torch.uint8))
-                for b, c in zip(back, caches))
-    nbytes = 2 * sh.num_segments * n * sh.page_bytes * args.steps
-    value = nbytes / t / 1e9
-    return {"impl": args.impl, "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": t / args.steps * 1e3, "higher_is_better": True, "dtype": "u8",
-            "config": {"workload": "cfg1 Qwen3-4B round trip: 36 layers x separate K/V "
-                                   "[1024,16,8,128] bf16 N(0,1) seed 0; 256 blocks out to "
-                                   "slots 0..255 then in to a fresh permutation, 72 swap "
-                                   "calls per direction",
-                       "api": "aegaeon.ops.swap (reference op)" if ref is not None
-                       else "aegaeon_b200.ops.swap -> kvx_swap",
-                       "transfer_mode": None if ref is not None else args.mode},
-            "bit_exact_round_trip": exact,
-            "e2e": {"value": nbytes / wall / 1e9, "unit": "GB/s",
-                    "h2d_bytes_per_step": nbytes // 2 // args.steps,
-                    "d2h_bytes_per_step": nbytes // 2 // args.steps}}
+    c = Cfg1(dev)
+    r = c.run(args.impl, args.steps, args.warmup, args.mode,
+              ref=_ref_module() if args.impl == "reference" else None)
+    line = _line_for(args, r, "cfg1 Qwen3-4B round trip: 36 layers x separate K/V "
+                     "[1024,16,8,128] bf16 N(0,1) seed 0; 256 blocks out to slots 0..255 then "
+                     "in to a fresh permutation, 72 swap calls per direction", args.impl)
+    line["e2e"].update({"h2d_bytes_per_step": c.step_bytes // 2,
+                        "d2h_bytes_per_step": c.step_bytes // 2})
+    return line
 
 
 def run_config4(args):
-    """Model-switch overlap: swap-in of 2048 cfg2 blocks (16 GiB) while a
-    Qwen1.5-14B TP-2 weight shard (14.17 GB bf16) is uploaded from
-    page-locked host memory in 64 MiB chunks on a second stream."""
     import torch
-
-    from aegaeon_b200 import _lib, swapper, workloads
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    sh = workloads.CFG2
-    n = 2048
-    gen = torch.Generator(device=dev).manual_seed(0)
-    ws = workloads.WeightShard()
-    w_dev = torch.empty(ws.nbytes, dtype=torch.uint8, device=dev)
-    w_host = torch.empty(ws.nbytes, dtype=torch.uint8).pin_memory()
-    w_host[:: 1 << 20].fill_(1)
-    in_ids = workloads.randperm(sh.num_blocks, 7)[:n]
-    s_kv, s_w = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    ref = _ref_module() if args.impl == "reference" else None
-    if ref is None:
-        pages = [torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
-                 for _ in range(sh.num_segments)]
-        segs, comp = swapper.make_segments([((f"l{i}",), sh.num_blocks * sh.page_bytes)
-                                            for i in range(sh.num_segments)], sh.num_blocks)
-        pool = torch.empty(n * comp, dtype=torch.uint8).pin_memory()
-        pool[:: 1 << 20].fill_(2)
-        sw = swapper.KVSwapper(0, segs, pages, [frozenset({0})] * sh.num_segments, [1],
-                               kv_swap=pool)
-        rows = list(range(n))
-
-        def step(_k):
-            sw.swap_blocks([0], rows, in_ids, [0] * n, [0] * n, [1] * n, [None], True,
-                           mode=args.mode, stream=s_kv)
-            _lib.check(_lib.lib().kvx_upload_chunked(w_dev.data_ptr(), w_host.data_ptr(),
-                                                     ws.nbytes, 64 << 20, s_w.cuda_stream))
-    else:
-        shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
-        caches = [torch.empty(shape, dtype=sh.dtype, device=dev) for _ in range(sh.num_segments)]
-        hosts = [torch.empty((n,) + shape[1:], dtype=sh.dtype).pin_memory() for _ in caches]
-        slots = list(range(n))
-        offs = [0]
-        for t in ws.tensors:
-            offs.append(offs[-1] + 2 * t)
-
-        def step(_k):
-            with torch.cuda.stream(s_kv):
-                for c, h in zip(caches, hosts):
-                    ref.swap(slots, in_ids, True, c, h)
-            with torch.cuda.stream(s_w):  # one copy per weight tensor (quick_loader.py:413)
-                for a, b in zip(offs[:-1], offs[1:]):
-                    w_dev[a:b].copy_(w_host[a:b], non_blocking=True)
-
-    for k in range(args.warmup):
-        step(k)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    t = _timed([s_kv, s_w], step, args.steps, dev)
-    wall = time.perf_counter() - t0
-    kv_bytes = n * sh.composite_bytes
-    per = t / args.steps
-    value = (kv_bytes + ws.nbytes) / per / 1e9
+    c = Cfg4(dev)
+    r = c.run(args.impl, args.steps, args.warmup, args.mode,
+              ref=_ref_module() if args.impl == "reference" else None)
     peaks = host_link_peaks(dev)
-    line = {"impl": args.impl, "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1e3,
-            "switch_ms": per * 1e3, "higher_is_better": True, "dtype": "u8",
-            "config": {"workload": "cfg4 switch overlap: swap-in of 2048 Llama-2-7B-shaped "
-                                   f"blocks ({kv_bytes} B) concurrent with a Qwen1.5-14B TP-2 "
-                                   f"bf16 weight shard ({ws.nbytes} B) uploaded on a second "
-                                   "stream",
-                       "weights": "64 MiB chunks, kvx_upload_chunked" if ref is None else
-                                  "one copy per weight tensor (quick_loader.py:413)"},
-            "roofline": {"bound": "host_link", "achieved": value, "peak": peaks["h2d_gbs"],
-                         "unit": "GB/s", "frac": value / peaks["h2d_gbs"],
-                         "peak_source": "measured live: 2 GiB page-locked H2D copy in 256 MiB "
-                                        "pieces"},
-            "e2e": {"value": (kv_bytes + ws.nbytes) * args.steps / wall / 1e9, "unit": "GB/s",
-                    "h2d_bytes_per_step": kv_bytes + ws.nbytes, "d2h_bytes_per_step": 0}}
+    line = _line_for(args, r, "cfg4 switch overlap: swap-in of 2048 Llama-2-7B-shaped blocks "
+                     f"({c.kv_bytes} B) concurrent with a Qwen1.5-14B TP-2 bf16 weight shard "
+                     f"({c.ws.nbytes} B) uploaded on a second stream", args.impl,
+                     {"switch_ms": r["switch_ms"],
+                      "roofline": {"bound": "host_link", "achieved": r["gbs"],
+                                   "peak": peaks["h2d_gbs"], "unit": "GB/s",
+                                   "frac": r["gbs"] / peaks["h2d_gbs"],
+                                   "peak_source": "measured live: 2 GiB page-locked H2D copy "
+                                                  "in 256 MiB pieces"}})
+    line["e2e"].update({"h2d_bytes_per_step": c.kv_bytes + c.ws.nbytes, "d2h_bytes_per_step": 0})
     return line
 
 
 def run_config5(args):
-    """Fragmented swap-out: Qwen1.5-MoE shape (24 layers x K/V, 64 KiB pages),
-    16384 entries, half in contiguous device runs of 1..32 blocks, half
-    isolated; host slots sequential.  One call per step; per-call latency."""
+    """Standalone configuration 5 on one GPU, all 24 layers unless the host
+    cannot page-lock 48 GiB (then fewer, stated)."""
     import torch
 
-    from aegaeon_b200 import ops, swapper, workloads
+    from aegaeon_b200 import workloads
 
-    dist_ = Dist.init(use_pg=args.impl == "kvx")
-    if args.impl == "reference" and dist_.rank != 0:
-        return None
-    dev = torch.device("cuda", dist_.local_rank)
-    sh = workloads.CFG5
-    n = 16384
-    avail = int([l for l in open("/proc/meminfo") if l.startswith("MemAvailable")][0].split()[1]) * 1024
-    fit = int(0.45 * avail / max(1, dist_.world if args.impl == "kvx" else 1) / sh.composite_bytes)
-    if fit < n:
-        n = max(1024, fit // 1024 * 1024)
-    ids, slots = workloads.fragmented_mapping(n, sh.num_blocks, seed=dist_.rank)
-    gen = torch.Generator(device=dev).manual_seed(dist_.rank)
-    ref = _ref_module() if args.impl == "reference" else None
-    s = torch.cuda.Stream(dev)
-    if ref is None:
-        pages = []
-        for _ in range(sh.num_segments):
-            t = torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
-            workloads.fill_segment(t, sh, gen)
-            pages.append(t)
-        segs, comp = swapper.make_segments([((f"l{i}",), sh.num_blocks * sh.page_bytes)
-                                            for i in range(sh.num_segments)], sh.num_blocks)
-        pool = torch.empty(n * comp, dtype=torch.uint8).pin_memory()
-        sw = swapper.KVSwapper(dev.index, segs, pages, [frozenset({0})] * sh.num_segments, [1],
-                               kv_swap=pool)
-
-        def step(_k):
-            sw.swap_blocks([0], ids, slots, [0] * n, [0] * n, [1] * n, [None], False,
-                           mode=args.mode, stream=s)
-    else:
-        shape = (sh.num_blocks, sh.block_size, sh.kv_heads, sh.head_dim)
-        caches = [torch.empty(shape, dtype=sh.dtype, device=dev).normal_(generator=gen)
-                  for _ in range(sh.num_segments)]
-        hosts = [torch.empty((n,) + shape[1:], dtype=sh.dtype).pin_memory() for _ in caches]
-
-        def step(_k):
-            with torch.cuda.stream(s):
-                for c, h in zip(caches, hosts):
-                    ref.swap(ids, slots, False, c, h)
-
-    for k in range(args.warmup):
-        step(k)
-    torch.cuda.synchronize()
-    dist_.barrier()
-    lat = []
-    t0 = time.perf_counter()
-    for k in range(args.steps):
-        lat.append(_timed([s], step, 1, dev))
-    wall = time.perf_counter() - t0
-    t = dist_.max(sum(lat))
-    nbytes = n * sh.composite_bytes
-    world = dist_.world if ref is None else 1
-    value = nbytes * args.steps * world / t / 1e9
-    line = None
-    if dist_.rank == 0:
-        line = {"impl": args.impl, "metric": METRIC, "value": value, "unit": "GB/s",
-                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-                "ms_per_step": t / args.steps * 1e3, "call_latency_ms": sorted(x * 1e3 for x in lat),
-                "higher_is_better": True, "dtype": "u8", "scaling": "weak",
-                "config": {"workload": f"cfg5 Qwen1.5-MoE-A2.7B fragmented swap-out: 24 layers x "
-                                       f"K/V 64 KiB pages, {n} entries (half in contiguous "
-                                       "device runs of 1..32 blocks, half isolated), host "
-                                       "slots sequential; one call per step",
-                           "entries": n,
-                           "api": "KVSwapper.swap_blocks -> kvx_swap_blocks" if ref is None
-                           else "aegaeon.ops.swap (reference op), 48 calls per step"},
-                "e2e": {"value": nbytes * args.steps * world / wall / 1e9, "unit": "GB/s",
-                        "h2d_bytes_per_step": 0, "d2h_bytes_per_step": nbytes * world}}
-    dist_.finish()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    layers = 24
+    try:
+        avail = int([l for l in open("/proc/meminfo")
+                     if l.startswith("MemAvailable")][0].split()[1]) * 1024
+        per_layer = 2 * 16384 * workloads.CFG5.page_bytes
+        layers = max(1, min(24, int(0.4 * avail // per_layer)))
+    except (OSError, IndexError, ValueError):
+        pass
+    c = Cfg5(dev, layers=layers)
+    r = c.run(args.impl, args.steps, args.warmup, args.mode,
+              ref=_ref_module() if args.impl == "reference" else None)
+    line = _line_for(args, r, f"cfg5 Qwen1.5-MoE-A2.7B fragmented swap-out: {layers} of 24 "
+                     "layers x K/V 64 KiB pages, 16384 entries (half in contiguous device runs "
+                     "of 1..32 blocks, half isolated), host slots sequential; one call per step",
+                     args.impl, {"call_latency_ms": r["call_ms"]})
+    line["e2e"].update({"h2d_bytes_per_step": 0, "d2h_bytes_per_step": c.call_bytes})
     return line
 
 
@@ -1484,7 +1974,7 @@ def main():
     args = parse_args()
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
-        if args.config in (1, 4, 7) and rank != 0:
+        if args.config in (1, 4, 5, 7) and rank != 0:
             return
         if args.config == 3:
             if args.impl != "reference":

@@ -23,6 +23,9 @@
  *   kvx_ipc_export /
  *   kvx_ipc_import      <- register_kvcache_mem_handles aegaeon/worker.py:2439-2451 (stub)
  *   kvx_upload_chunked  <- weight upload during switch aegaeon/loader/quick_loader.py:398-444
+ *   kvx_upload_weights  <- pipeline_storage_transfer
+ *                          quick_model_loader/quick_model_loader/model_loader.py:348-369,
+ *                          load_tensors_content aegaeon/loader/quick_loader.py:326-340
  *   kvx_byte_extent     <- byte_extent_for_kernel_blocks aegaeon/cache_transfer.py:138-165
  */
 #ifndef KVX_H_
@@ -190,6 +193,30 @@ int kvx_event_release(kvx_event* event);
  * aegaeon/loader/quick_loader.py:398-444.                                    */
 int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,
                        uint64_t chunk_bytes, void* stream);
+
+/* ---- f1: weight upload of a model switch ----------------------------------
+ * Copies num_buffers host buffers (weight storages) into device buffers of
+ * the current device in pieces of chunk_bytes, in order, on `stream`.
+ *  * Page-locked (or managed) sources: one cudaMemcpyAsync per piece; the
+ *    call returns once they are queued.
+ *  * Pageable sources: through two page-locked bounce buffers of chunk_bytes
+ *    owned by the library (allocated on first use).  host_threads threads copy
+ *    piece k+1 into one bounce buffer while the copy engine moves piece k out
+ *    of the other, the two-stage pipeline of the reference's
+ *    pipeline_storage_transfer (pageable -> pinned -> device, cut into
+ *    pieces).  The call returns when the last piece is queued; it blocks only
+ *    to reuse a bounce buffer.
+ * Destinations must be device memory of the current device.  Errors:
+ * KVX_ERR_INVALID_ARGUMENT (null pointers, chunk_bytes 0, a destination that
+ * is not device memory of the current device), KVX_ERR_CUDA.
+ * Replaces: pipeline_storage_transfer,
+ * quick_model_loader/quick_model_loader/model_loader.py:348-369, and the
+ * per-storage slice_storage.copy_(non_blocking=True) of load_tensors_content,
+ * aegaeon/loader/quick_loader.py:326-340 (64 MiB cuts as in the disabled
+ * variant at :398-444).                                                      */
+int kvx_upload_weights(void* const* dst_device, const void* const* src_host,
+                       const uint64_t* bytes, int64_t num_buffers, uint64_t chunk_bytes,
+                       int host_threads, void* stream);
 
 /* ---- a3: extent arithmetic (host only, no GPU needed) ---------------------
  * (first, count) kernel blocks of a page of page_bytes split into
