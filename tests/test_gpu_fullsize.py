@@ -109,6 +109,7 @@ def full_shape_parity(dev, ref, sh, num_blocks, out_ids, in_ids, mode):
         assert torch.equal(rows[:, s], u8(ref_host[s]).to(dev).view(n, sh.page_bytes)), ("rows", s)
     del rows
     back_pages = [torch.zeros_like(p) for p in pages]
+    torch.cuda.synchronize()  # the fills run on the current stream, the swap on its own
     sw_back = swapper.KVSwapper(dev.index, segs, back_pages, [frozenset({0})] * sh.num_segments,
                                 [1], kv_swap=pool)
     sw_back.swap_blocks([0], slots, in_ids, z, z, one, [None], True, mode=mode).synchronize()
