@@ -311,6 +311,10 @@ int staging_get(DeviceState* st, int idx, size_t want, cudaStream_t s,
 // ---- kernel launch ---------------------------------------------------------
 enum class Path { kHostSrc, kHostDst, kDevice, kPeer };
 
+// Both sides device memory: this GPU's own, or a peer's mapped over NVLink
+// (the TMA bulk kernel may serve these; host memory goes through the SMs).
+bool device_side(Path p) { return p == Path::kDevice || p == Path::kPeer; }
+
 int ctas_for(const DeviceState* st, Path p, const Tunables& tn) {
   if (p == Path::kHostSrc || p == Path::kHostDst)
     return int(tn.sm_ctas_host > 0 ? tn.sm_ctas_host : st->sms);
@@ -555,7 +559,7 @@ int run_sm(DeviceState* st, const std::vector<Copy>& copies,
     std::vector<Copy> w(copies.begin() + begin, copies.begin() + end);
     begin = end;
     coalesce(&w);
-    const bool bulk = allow_bulk && path == Path::kDevice && all_aligned16(w);
+    const bool bulk = allow_bulk && device_side(path) && all_aligned16(w);
     int rc = add_items(&up, &launches, w, path, bulk);
     if (rc) return rc;
   }
@@ -567,7 +571,7 @@ int run_sm_grid(DeviceState* st, GridPlan* p, Path path, bool allow_bulk, cudaSt
                 const Tunables& tn) {
   Upload up;
   std::vector<Launch> launches;
-  const bool bulk = allow_bulk && path == Path::kDevice && grid_aligned16(*p);
+  const bool bulk = allow_bulk && device_side(path) && grid_aligned16(*p);
   int rc = add_grid(&up, &launches, p, path, bulk);
   if (rc) return rc;
   if (!bulk && tn.inline_lists && fits_inline(*p))
@@ -795,6 +799,18 @@ std::vector<Copy> grid_copies(GridPlan p) {
   return v;
 }
 
+// The same copies ordered by source address and coalesced, for one
+// copy-engine copy per extent.  A grid plan's copies never conflict (distinct
+// targets, no overlap between the sides), so their order is free; the
+// entry-major expansion puts different segments next to each other, which
+// never coalesce, while consecutive blocks of one segment do.
+std::vector<Copy> grid_extents(const GridPlan& p) {
+  std::vector<Copy> v = grid_copies(p);
+  std::sort(v.begin(), v.end(), [](const Copy& a, const Copy& b) { return a.src < b.src; });
+  coalesce(&v);
+  return v;
+}
+
 // Host memory facts for the SM path.
 struct HostInfo {
   bool mapped = false;     // device can address it
@@ -883,8 +899,7 @@ int execute_host_copies(DeviceState* st, std::vector<Copy>& copies, bool is_swap
 // most 16 copies are expanded to check.
 bool direct_copies(const GridPlan& p, const Tunables& tn, std::vector<Copy>* out) {
   if (tn.direct_max <= 0 || p.entries.size() * p.segs.size() > 16) return false;
-  std::vector<Copy> v = grid_copies(p);
-  coalesce(&v);
+  std::vector<Copy> v = grid_extents(p);
   if (v.size() > uint64_t(tn.direct_max)) return false;
   *out = std::move(v);
   return true;
@@ -937,7 +952,8 @@ int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
                          tn);
     }
   } else if (mode == KVX_MODE_CE_EXTENT) {
-    if (expanded.empty()) expanded = grid_copies(*p);
+    // (already set, ordered and coalesced, when AUTO chose direct copies)
+    if (expanded.empty()) expanded = grid_extents(*p);
     rc = run_ce_extent(expanded, {expanded.size()}, s);
   } else {
     return set_error(KVX_ERR_INVALID_ARGUMENT, "unknown transfer mode " + std::to_string(mode));
@@ -1392,11 +1408,13 @@ int kvx_migrate_blocks(kvx_layout* source, kvx_layout* target, int64_t num_entri
   if (mode == KVX_MODE_AUTO) mode = KVX_MODE_SM;
   const Path path = local ? Path::kDevice : Path::kPeer;
   if (mode == KVX_MODE_CE || mode == KVX_MODE_CE_EXTENT) {
-    if (grid) copies = grid_copies(gp);
+    if (grid) copies = grid_extents(gp);
     rc = run_ce_extent(copies, grid ? std::vector<size_t>{copies.size()} : split_waves(copies), s);
     mode = KVX_MODE_CE_EXTENT;
   } else if (mode == KVX_MODE_SM || mode == KVX_MODE_SM_BULK) {
-    const bool bulk = mode == KVX_MODE_SM_BULK && local;
+    // TMA bulk copies also cross NVLink: plain (non-multicast) bulk loads
+    // from a peer's pages (pull) or bulk stores into them (push).
+    const bool bulk = mode == KVX_MODE_SM_BULK;
     if (grid)
       rc = run_sm_grid(st, &gp, path, bulk, s, tn);
     else

@@ -70,9 +70,10 @@ def parse_args():
                         "restatement of Worker.swap_blocks' hot loop (worker.py:2270-2329: "
                         "one torch copy_ per segment and block into composite host rows), "
                         "which cannot run as-is without Ray and vLLM")
-    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7], default=2,
+    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8], default=2,
                    help="BASELINE.json configuration (2 = the headline line; 3 is the "
-                        "migration object of the N>=2 line; 7 = latency of small swap calls)")
+                        "migration object of the N>=2 line; 7 = latency of small swap calls; "
+                        "8 = migration transfer forms at N>=2)")
     p.add_argument("--mode", default="auto", help="transfer mode: auto|sm|ce|ce_extent")
     p.add_argument("--blocks", type=int, default=1024, help="blocks per direction per step")
     p.add_argument("--cache-blocks", type=int, default=4096,
@@ -709,7 +710,7 @@ def _ipc_event_ordering(dist_, dev, sw, pages, page: int, plan, is_src: bool, pa
 
 
 def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull",
-                    ipc_check: bool = False) -> dict:
+                    ipc_check: bool = False, mode: str = "auto", extras: bool = True) -> dict:
     """Configuration 3 at N >= 2: pairs (i, i + N/2), rank i the prefill side.
     pull: the decode rank maps the prefill rank's cache and copies the blocks
     in (loads over NVLink); push: the prefill rank stores them into the
@@ -746,7 +747,7 @@ def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull"
     def run():
         if active:
             sw.migrate_blocks([pair], partner, plan.source_ids, plan.target_ids, None,
-                              direction=direction, stream=stream)
+                              direction=direction, stream=stream, mode=mode)
 
     for _ in range(warmup):
         run()
@@ -763,6 +764,15 @@ def migration_bench(dist_, dev, steps: int, warmup: int, direction: str = "pull"
     # Exact parity of the timed migrations, position-keyed across the pair.
     parity = _pair_exact(dist_, dev, pages, sh.page_bytes,
                          plan.source_ids if is_src else plan.target_ids, is_src, partner)
+    if not extras:
+        sw.close()
+        del pages
+        torch.cuda.empty_cache()
+        per_pair = nbytes * steps / t / 1e9
+        return {"per_pair_gbs": per_pair, "frac_of_nominal_900": per_pair / 900.0,
+                "peer_copy_gbs": peer_peak["per_pair_gbs"],
+                "frac_of_measured_peer_copy": per_pair / peer_peak["per_pair_gbs"],
+                "bit_exact": parity}
     # Small calls: the plan's first n blocks (all 56 segments), as a decode
     # rank pulls a short request; µs per call, device time, max over ranks.
     small = {}
@@ -1883,6 +1893,44 @@ def run_config6(args):
             "per_length": results}
 
 
+def run_config8(args):
+    """Transfer forms of the configuration-3 migration at N >= 2 (pairs
+    (i, i+N/2)): pull and push through the vector kernel (KVX_MODE_SM at
+    several CTA counts) and through the TMA bulk kernel (KVX_MODE_SM_BULK),
+    each timed like the default run's migration object and checked byte for
+    byte across the pair.  One JSON line on rank 0."""
+    import torch
+
+    from aegaeon_b200 import _lib
+
+    dist_ = Dist.init(use_pg=True)
+    if dist_.world < 2:
+        emit({"impl": args.impl, "note": "config 8 needs torchrun with 2 or more ranks"})
+        return
+    dev = torch.device("cuda", dist_.local_rank)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    variants = [("sm", k * sms) for k in (1, 2, 4, 8, 16)] + [("sm_bulk", None)]
+    out = {}
+    for direction in ("pull", "push"):
+        for mode, ctas in variants:
+            if ctas:
+                _lib.configure(sm_ctas_dev=ctas)
+            r = migration_bench(dist_, dev, steps=args.steps, warmup=args.warmup,
+                                direction=direction, mode=mode, extras=False)
+            key = f"{direction}_{mode}" + (f"_{ctas}ctas" if ctas else "")
+            out[key] = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in r.items()}
+    _lib.configure(sm_ctas_dev=4 * sms)
+    if dist_.rank == 0:
+        best = max(out, key=lambda k: out[k]["per_pair_gbs"])
+        emit({"impl": args.impl, "metric": "P->D migration GB/s per GPU pair (cfg3)",
+              "value": out[best]["per_pair_gbs"], "unit": "GB/s", "n_gpus": dist_.world,
+              "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+              "dtype": "u8", "config": {"workload": "cfg3 Qwen2.5-7B P->D migration, pairs "
+                                                    "(i, i+N/2), 8 requests per pair"},
+              "best": best, "variants": out})
+    dist_.finish()
+
+
 SMALL_CALL_BLOCKS = (1, 2, 4, 16, 64, 256)
 
 
@@ -1983,6 +2031,9 @@ def main():
                 return
             if rank == 0:
                 emit(run_config3_reference(args))
+            return
+        if args.config == 8:
+            run_config8(args)
             return
         if args.config == 6:
             if rank == 0:

@@ -62,8 +62,9 @@ extern "C" {
                             /* side through its device-mapped address          */
 #define KVX_MODE_CE 2       /* copy engines over coalesced runs; HBM side      */
                             /* gathered into / scattered from a staging area   */
-#define KVX_MODE_SM_BULK 3  /* device<->device only: TMA bulk copies through   */
-                            /* shared memory                                   */
+#define KVX_MODE_SM_BULK 3  /* device<->device only (local, or a peer's pages  */
+                            /* mapped over NVLink): TMA bulk copies through    */
+                            /* shared memory, no multicast                     */
 #define KVX_MODE_CE_EXTENT 4 /* one copy-engine copy per coalesced extent, no */
                             /* staging (fast when extents are already large)   */
 
@@ -138,8 +139,10 @@ int kvx_swap_blocks(kvx_layout* layout, int64_t num_entries,
  * which must be able to address both layouts' pages: its own memory, and a
  * peer's memory mapped into this process with kvx_ipc_import.  Pull (run on
  * the target GPU, source pages imported) and push (run on the source GPU,
- * target pages imported) are both valid; each 16-byte load or store that
- * crosses NVLink is a plain peer access (no multicast).  The segment tables
+ * target pages imported) are both valid; each load or store that crosses
+ * NVLink is a plain peer access (no multicast): 16/32-byte vector accesses
+ * in KVX_MODE_SM (AUTO), bulk copies through shared memory in
+ * KVX_MODE_SM_BULK.  The segment tables
  * of the two layouts must agree in count, page sizes and owners, and their
  * group tables must be equal.
  * Fills: Worker.migrate_blocks, worker.py:2420-2430 (NotImplementedError in
