@@ -12,7 +12,10 @@ Mirrors the planning half of the reference's block manager
 * ``plan_swap_lists`` (block_manager.py:1434-1478): the parallel
   src/dst/group/first/valid lists that ``swap_blocks`` consumes, with
   zero-length entries kept in the destination tables but dropped from the
-  copy lists.
+  copy lists;
+* ``plan_move_requests`` (block_manager.py:1355-1478): the whole list-building
+  step of ``BlockManager.move_requests`` (request de-duplication, location,
+  shape and cache-group checks, one destination reservation, table updates).
 """
 
 from __future__ import annotations
@@ -266,3 +269,100 @@ def plan_swap_lists(plans: Sequence[Tuple[BlockTable, int]],
             out.valid_kernel_blocks.append(count)
         out.destination_tables.append(bt.moved_group_blocks(processed, targets))
     return out
+
+
+@dataclass
+class MovePlan:
+    """Everything ``move_requests`` decides for one batch: the requests that
+    move, where the transfer runs, the parallel copy lists and the source
+    ids to release once the move has completed."""
+
+    swapped_request_ids: List[int]
+    source_location: int
+    target_location: int
+    block_shape: Tuple[int, ...]
+    engine_id: int
+    is_swap_in: bool
+    is_migration: bool
+    source_block_ids: List[int]
+    target_block_ids: List[int]
+    group_ids: List[int]
+    first_kernel_blocks: List[int]
+    valid_kernel_blocks: List[int]
+    release_source_block_ids: List[int]
+
+
+def plan_move_requests(block_tables, requests, target_location: int, gpu_cache_groups,
+                       reserve, *, allow_migration: bool = False) -> Optional[MovePlan]:
+    """The list-building half of ``BlockManager.move_requests``
+    (block_manager.py:1355-1478), with the same checks and results.
+
+    ``block_tables`` maps request id -> BlockTable; ``requests`` are objects
+    with ``request_id`` and ``get_first_new_token_index()``;
+    ``gpu_cache_groups`` maps a GPU location to its cache-group tuple;
+    ``reserve(n, location, block_shape)`` returns n free destination ids
+    (the block manager's ``_get_free_blocks``).  Repeated requests count
+    once and requests already at ``target_location`` are left alone.  The
+    whole destination is reserved in one call before any table changes; then
+    every moved table gets its destination ids and the target location.
+    Retained pages with nothing to copy keep a destination id but stay out of
+    the copy lists.  Returns None when nothing moves.
+
+    GPU -> GPU moves raise NotImplementedError as in the reference unless
+    ``allow_migration`` is set; then they produce a migration plan for
+    ``KVSwapper.migrate_blocks`` run on the target GPU (pull).
+    """
+    moving = []  # (table, processed tokens, transfer entries)
+    swapped: List[int] = []
+    release: List[int] = []
+    cur_loc: Optional[int] = None
+    shape: Optional[Tuple[int, ...]] = None
+    seen = set()
+    for req in requests:
+        rid = req.request_id
+        if rid in seen:
+            continue
+        seen.add(rid)
+        table = block_tables.get(rid, None)
+        assert table, f"request {rid} not allocated"
+        here = table.location
+        if here == target_location:
+            continue
+        if here >= 0 and target_location >= 0 and not allow_migration:
+            raise NotImplementedError("Migration is not implemented")
+        if cur_loc is not None:
+            assert here == cur_loc, f"request {rid} is on {here}; expected {cur_loc}"
+        if shape is not None:
+            assert table.block_shape == shape, f"request {rid}'s shape is not {shape}"
+        cur_loc, shape = here, table.block_shape
+        swapped.append(rid)
+        if target_location >= 0 and table.cache_groups != gpu_cache_groups[target_location]:
+            raise ValueError(f"request {rid} cache groups do not match target engine "
+                             f"#{target_location}")
+        processed = req.get_first_new_token_index()
+        moving.append((table, processed, table.transfer_entries(processed)))
+        release.extend(table.blocks)
+    if not swapped:
+        return None
+    targets = list(reserve(sum(len(e) for _, _, e in moving), target_location, shape))
+    plan = MovePlan(swapped, cur_loc, target_location, shape,
+                    target_location if target_location >= 0 else cur_loc,
+                    target_location >= 0 and cur_loc < 0, cur_loc >= 0 and target_location >= 0,
+                    [], [], [], [], [], release)
+    new_tables = []
+    at = 0
+    for table, processed, entries in moving:
+        mine = targets[at:at + len(entries)]
+        at += len(entries)
+        for (gid, _, block_id, first, count), dst in zip(entries, mine):
+            if count > 0:
+                plan.source_block_ids.append(block_id)
+                plan.target_block_ids.append(dst)
+                plan.group_ids.append(gid)
+                plan.first_kernel_blocks.append(first)
+                plan.valid_kernel_blocks.append(count)
+        new_tables.append(table.moved_group_blocks(processed, mine))
+    for (table, _, _), groups in zip(moving, new_tables):
+        table.group_blocks = groups
+        table.location = target_location
+    return plan

@@ -394,30 +394,44 @@ class SwapBench:
         return _lib.kernel_timing_read()
 
     def timed_e2e(self, steps: int, mode: str):
-        """Wall clock through the public API from block tables."""
+        """Wall clock through the public API from block tables: the
+        move_requests list building (plan_move_requests) for the outgoing and
+        the incoming requests, then KVSwapper.swap_blocks per direction."""
         from aegaeon_b200 import block_table as bt
 
-        torch = self.torch
         group = (bt.CacheGroupConfig("attention", 16, 16),)
         per_req = 16  # 256-token requests: 16 full pages each
+
+        class Req:
+            def __init__(self, rid):
+                self.request_id = rid
+
+            def get_first_new_token_index(self):
+                return 256
+
         t0 = time.perf_counter()
         for k in range(steps):
             out_ids, rows_out, rows_in, in_ids = self.step_lists(1000 + k)
             n_req = self.per_dir // per_req
-            out_plans = [(bt.BlockTable(0, (1,), group, [out_ids[r * per_req:(r + 1) * per_req]]),
-                          256) for r in range(n_req)]
-            in_plans = [(bt.BlockTable(-1, (1,), group, [rows_in[r * per_req:(r + 1) * per_req]]),
-                         256) for r in range(n_req)]
-            lo = bt.plan_swap_lists(out_plans, rows_out)
-            li = bt.plan_swap_lists(in_plans, in_ids)
-            e_out = self.sw.swap_blocks(list(range(n_req)), lo.source_block_ids,
+            tables = {r: bt.BlockTable(0, (1,), group, [out_ids[r * per_req:(r + 1) * per_req]])
+                      for r in range(n_req)}
+            tables.update({n_req + r: bt.BlockTable(-1, (1,), group,
+                                                    [rows_in[r * per_req:(r + 1) * per_req]])
+                           for r in range(n_req)})
+            lo = bt.plan_move_requests(tables, [Req(r) for r in range(n_req)], -1,
+                                       {0: group}, lambda n, loc, shape: rows_out[:n])
+            li = bt.plan_move_requests(tables, [Req(n_req + r) for r in range(n_req)], 0,
+                                       {0: group}, lambda n, loc, shape: in_ids[:n])
+            e_out = self.sw.swap_blocks(lo.swapped_request_ids, lo.source_block_ids,
                                         lo.target_block_ids, lo.group_ids,
                                         lo.first_kernel_blocks, lo.valid_kernel_blocks,
-                                        [None] * n_req, False, mode=mode, stream=self.s_out)
-            e_in = self.sw.swap_blocks(list(range(n_req)), li.source_block_ids,
+                                        [None] * n_req, lo.is_swap_in, mode=mode,
+                                        stream=self.s_out)
+            e_in = self.sw.swap_blocks(li.swapped_request_ids, li.source_block_ids,
                                        li.target_block_ids, li.group_ids,
                                        li.first_kernel_blocks, li.valid_kernel_blocks,
-                                       [None] * n_req, True, mode=mode, stream=self.s_in)
+                                       [None] * n_req, li.is_swap_in, mode=mode,
+                                       stream=self.s_in)
             self.s_out.wait_event(e_in)
             self.s_in.wait_event(e_out)
         self.s_out.synchronize()
@@ -1099,7 +1113,8 @@ def run_kvx(args):
                 "unit": "GB/s",
                 "h2d_bytes_per_step": per_dir * workloads.CFG2.composite_bytes * dist_.world,
                 "d2h_bytes_per_step": per_dir * workloads.CFG2.composite_bytes * dist_.world,
-                "api": "block tables -> plan_swap_lists -> KVSwapper.swap_blocks -> stream sync",
+                "api": "block tables -> plan_move_requests (move_requests list building) -> "
+                       "KVSwapper.swap_blocks -> stream sync",
                 "seconds": t_e2e,
             },
             "gpu_launches": launches,

@@ -13,6 +13,9 @@ Fixtures:
   block_tables.json  BlockTable.transfer_entries / moved_group_blocks /
                      swap_metadata and CacheGroupRuntimeConfig extents from
                      block_manager.py (``ray`` stubbed; it is not used there)
+  move_requests.json BlockManager.move_requests (block_manager.py:1355-1525)
+                     run on a stub manager: request lists, reservations,
+                     swap_blocks arguments, tables and move events per move
   swap_blocks.json   Worker.swap_blocks (worker.py:2204-2349), extracted from
                      the source with ``ast`` and executed on CPU tensors with
                      CUDA streams/events stubbed, on seeded byte contents:
@@ -274,6 +277,147 @@ def gen_swap_blocks(bm) -> dict:
     return {"scenarios": scenarios}
 
 
+class _Req:
+    """The two members move_requests reads from a request."""
+
+    def __init__(self, request_id, processed):
+        self.request_id = request_id
+        self._processed = processed
+
+    def get_first_new_token_index(self):
+        return self._processed
+
+
+def gen_move_requests(bm) -> dict:
+    """BlockManager.move_requests (block_manager.py:1355-1525) run on a stub
+    manager: the reference's own BlockTable objects, a free-block reservation
+    that hands out recorded ids, and a worker RPC that records its
+    arguments.  Each scenario is a sequence of moves on one manager; per move
+    the fixture keeps the request list, the target, the reservation calls,
+    the swap_blocks arguments, the tables afterwards, the move event and the
+    outcome (return value or exception)."""
+    import asyncio
+    import itertools
+    from collections import defaultdict
+
+    rng = np.random.default_rng(17)
+    group_specs = {
+        "uniform": [("attention", 16, 16, None)],
+        "hybrid": [("attention", 528, 16, None), ("mamba_none", 528, 528, None)],
+        "window": [("attention", 64, 16, 40), ("attention", 16, 16, None)],
+        "w1": [("attention", 32, 16, 1)],
+    }
+
+    def groups_of(name):
+        return tuple(bm.CacheGroupConfig(*g) for g in group_specs[name])
+
+    def new_manager(gpu_groups):
+        calls = {"reserve": [], "rpc": []}
+        next_id = itertools.count(20000)
+
+        async def get_free(n, location, shape):
+            ids = [next(next_id) for _ in range(n)]
+            calls["reserve"].append([n, location, list(shape), ids])
+            return ids
+
+        def rpc_for(engine):
+            def call(method, *args):
+                calls["rpc"].append([engine, method, [list(a) if isinstance(a, list) else a
+                                                      for a in args]])
+                return f"event-refs-{len(calls['rpc'])}"
+            return call
+
+        mgr = types.SimpleNamespace(
+            block_tables={}, gpu_cache_groups={k: groups_of(v) for k, v in gpu_groups.items()},
+            _get_free_blocks=get_free, latest_events={},
+            remote_callables=defaultdict(lambda: None), event_counter=itertools.count(),
+            move_gpu_num_blocks=defaultdict(int), move_events_gpu=defaultdict(list),
+            move_cpu_num_blocks=defaultdict(int), move_events_cpu=defaultdict(list))
+        for loc in list(gpu_groups) + [-1]:
+            mgr.remote_callables[loc] = rpc_for(loc)
+        return mgr, calls
+
+    def add_table(mgr, rid, loc, shape, gname, processed):
+        groups = groups_of(gname)
+        blocks = []
+        for g in groups:
+            n = g.table_blocks_for_tokens(max(processed + int(rng.integers(0, 20)), 1))
+            ids = [int(x) for x in rng.choice(10000, size=n, replace=False)]
+            if g.sliding_window is not None and n > 2:
+                ids[0] = bm.LOGICAL_NULL_BLOCK_ID
+            blocks.append(ids)
+        mgr.block_tables[rid] = bm.BlockTable(loc, tuple(shape), groups, blocks)
+        return {"request_id": rid, "location": loc, "block_shape": list(shape), "groups": gname,
+                "group_blocks": [list(b) for b in blocks]}
+
+    def snapshot(mgr):
+        return {str(rid): {"location": t.location, "group_blocks": [list(b) for b in t.group_blocks]}
+                for rid, t in sorted(mgr.block_tables.items())}
+
+    def move(mgr, calls, reqs, target):
+        calls["reserve"].clear()
+        calls["rpc"].clear()
+        requests = [_Req(rid, p) for rid, p in reqs]
+        try:
+            result = {"ok": asyncio.run(bm.BlockManager.move_requests(mgr, requests, target))}
+        except Exception as e:  # noqa: BLE001 - the exception is the recorded result
+            result = {"error": type(e).__name__, "message": str(e)}
+        events = [[ev.serial, ev.source_location, ev.target_location, list(ev.source_blocks),
+                   [r.request_id for r in ev.requests]]
+                  for d in (mgr.move_events_gpu, mgr.move_events_cpu) for evs in d.values()
+                  for ev in evs]
+        return {"requests": [list(r) for r in reqs], "target": target, "result": result,
+                "reserve": [list(c) for c in calls["reserve"]],
+                "rpc": [list(c) for c in calls["rpc"]], "tables": snapshot(mgr),
+                "move_events": events,
+                "move_gpu_num_blocks": {str(k): v for k, v in mgr.move_gpu_num_blocks.items()},
+                "move_cpu_num_blocks": {str(list(k)): v for k, v in mgr.move_cpu_num_blocks.items()},
+                "latest_events": sorted(mgr.latest_events)}
+
+    scenarios = []
+    for gname in group_specs:
+        mgr, calls = new_manager({0: gname, 1: gname})
+        tables = []
+        procs = {}
+        for rid in range(6):
+            p = int(rng.choice([0, 1, 15, 16, 17, 63, 200, 529, 1100]))
+            procs[rid] = p
+            tables.append(add_table(mgr, rid, 0 if rid < 5 else -1, (2, 16), gname, p))
+        moves = [
+            # out: duplicates counted once; request 5 is already on the CPU
+            move(mgr, calls, [(0, procs[0]), (1, procs[1]), (0, procs[0]), (2, procs[2]),
+                              (5, procs[5])], -1),
+            # in again, with a request already on the GPU mixed in
+            move(mgr, calls, [(1, procs[1]), (3, procs[3]), (0, procs[0])], 0),
+            # nothing to do
+            move(mgr, calls, [(0, procs[0]), (3, procs[3])], 0),
+            # GPU -> GPU is not implemented in the reference
+            move(mgr, calls, [(4, procs[4])], 1),
+            # mixed source locations
+            move(mgr, calls, [(4, procs[4]), (2, procs[2])], 1),
+            # unknown request
+            move(mgr, calls, [(99, 0)], -1),
+            # out and back in with more tokens processed
+            move(mgr, calls, [(4, procs[4] + 40), (3, procs[3] + 40)], -1),
+            move(mgr, calls, [(3, procs[3] + 41), (4, procs[4] + 41), (5, procs[5])], 0),
+        ]
+        scenarios.append({"groups": gname, "gpu_groups": {"0": gname, "1": gname},
+                          "tables": tables, "moves": moves})
+    # shape mismatch, and a target engine with other cache groups
+    mgr, calls = new_manager({0: "uniform", 1: "window"})
+    tables = [add_table(mgr, 0, 0, (2, 16), "uniform", 40),
+              add_table(mgr, 1, 0, (2, 8), "uniform", 40),
+              add_table(mgr, 2, -1, (2, 16), "uniform", 40),
+              add_table(mgr, 3, 1, (2, 16), "uniform", 40)]
+    moves = [move(mgr, calls, [(0, 40), (1, 40)], -1),
+             move(mgr, calls, [(0, 40), (3, 40)], -1),
+             move(mgr, calls, [(2, 40)], 1),
+             move(mgr, calls, [(2, 40)], 0)]
+    scenarios.append({"groups": "mixed", "gpu_groups": {"0": "uniform", "1": "window"},
+                      "tables": tables, "moves": moves})
+    return {"group_specs": group_specs, "scenarios": scenarios}
+
+
 def main() -> None:
     if not os.path.isdir(os.path.join(REF, "aegaeon")):
         sys.exit(f"reference checkout not found at {REF}")
@@ -290,6 +434,7 @@ def main() -> None:
                 "extents.json": gen_extents(ct),
                 "block_tables.json": gen_block_tables(bm),
                 "swap_blocks.json": gen_swap_blocks(bm),
+                "move_requests.json": gen_move_requests(bm),
             }
         finally:
             os.chdir(cwd)
@@ -299,7 +444,9 @@ def main() -> None:
                        "reference_files": {
                            "extents.json": "aegaeon/cache_transfer.py",
                            "block_tables.json": "aegaeon/block_manager.py",
-                           "swap_blocks.json": "aegaeon/worker.py (Worker.swap_blocks)"}[name],
+                           "swap_blocks.json": "aegaeon/worker.py (Worker.swap_blocks)",
+                           "move_requests.json": "aegaeon/block_manager.py "
+                                                 "(BlockManager.move_requests)"}[name],
                        "data": data}, f, separators=(",", ":"))
         print(name, os.path.getsize(os.path.join(OUT, name)), "bytes")
 
