@@ -14,7 +14,7 @@ cache (weak scaling, no collective on the data path).
 Printed JSON line (rank 0): ``value`` is the device-timed box aggregate GB/s
 (CUDA events on the launching streams, max over ranks); ``e2e`` is the same
 metric timed by the wall clock through the public API from block tables
-(plan_swap_lists -> KVSwapper.swap_blocks -> wait), with the payload crossing
+(plan_move_requests -> KVSwapper.swap_blocks -> wait), with the payload crossing
 the host link inside the timed region.  ``roofline`` is the device-side
 gather kernel against the measured HBM copy peak, with the binding host-link
 roofline nested in it (``roofline.host_link``: the measured concurrent
@@ -70,10 +70,11 @@ def parse_args():
                         "restatement of Worker.swap_blocks' hot loop (worker.py:2270-2329: "
                         "one torch copy_ per segment and block into composite host rows), "
                         "which cannot run as-is without Ray and vLLM")
-    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8], default=2,
+    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8, 9], default=2,
                    help="BASELINE.json configuration (2 = the headline line; 3 is the "
                         "migration object of the N>=2 line; 7 = latency of small swap calls; "
-                        "8 = migration transfer forms at N>=2)")
+                        "8 = migration transfer forms at N>=2; 9 = fragmented host slots, both "
+                        "directions)")
     p.add_argument("--mode", default="auto", help="transfer mode: auto|sm|ce|ce_extent")
     p.add_argument("--blocks", type=int, default=1024, help="blocks per direction per step")
     p.add_argument("--cache-blocks", type=int, default=4096,
@@ -1970,6 +1971,110 @@ def run_config8(args):
     dist_.finish()
 
 
+def run_config9(args):
+    """Fragmented host slots with both directions active.  The reference's
+    CPU slab allocator hands out host slots from a free list
+    (block_manager.py:942-1031), so after some churn the slots of one swap
+    are scattered rows of the pool.  Workload: a Qwen2.5-7B-shaped cache (28
+    layers x K/V, 16 KiB pages: 896 KiB host rows, below the 1 MiB host run
+    that AUTO needs for the copy engines); per step 1024 random blocks out to 1024
+    shuffled rows of a 4096-row pool and 1024 other blocks in from other
+    shuffled rows, on the two swap streams at once.  Every transfer-mode
+    pair (swap-out mode, swap-in mode) is timed and its last step checked
+    byte for byte; GB/s both directions together against the live
+    bidirectional copy-engine peak."""
+    import torch
+
+    from aegaeon_b200 import _lib, swapper, workloads
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    sh = workloads.CFG3
+    n, rows_total = 1024, 4096
+    gen = torch.Generator(device=dev).manual_seed(0)
+    pages = []
+    for _ in range(sh.num_segments):
+        t = torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
+        workloads.fill_segment(t, sh, gen)
+        pages.append(t)
+    segs, comp = swapper.make_segments([((f"l{i}",), sh.num_blocks * sh.page_bytes)
+                                        for i in range(sh.num_segments)], sh.num_blocks)
+    pool = torch.empty(rows_total * comp, dtype=torch.uint8, pin_memory=True)
+    fill = torch.empty(GIB, dtype=torch.uint8, device=dev)
+    for o in range(0, pool.numel(), GIB):
+        fill.random_(0, 256, generator=gen)
+        pool[o:o + GIB].copy_(fill[:pool.numel() - o])
+    del fill
+    sw = swapper.KVSwapper(0, segs, pages, [frozenset({0})] * sh.num_segments, [1], kv_swap=pool)
+    peaks = host_link_peaks(dev)
+    z, one = [0] * n, [1] * n
+
+    def lists(k):
+        blocks = workloads.randperm(sh.num_blocks, 900 + k)
+        rows = workloads.randperm(rows_total, 500 + k)
+        return blocks[:n], rows[:n], rows[n:2 * n], blocks[n:2 * n]
+
+    def step(k, m_out, m_in):
+        out_b, out_r, in_r, in_b = lists(k)
+        e_out = sw.swap_blocks([0], out_b, out_r, z, z, one, [None], False, mode=m_out,
+                               stream=sw.swap_out_stream)
+        mo = _lib.last_mode_name()
+        e_in = sw.swap_blocks([1], in_r, in_b, z, z, one, [None], True, mode=m_in,
+                              stream=sw.swap_in_stream)
+        mi = _lib.last_mode_name()
+        sw.swap_out_stream.wait_event(e_in)
+        sw.swap_in_stream.wait_event(e_out)
+        return mo, mi
+
+    def check(k) -> bool:
+        out_b, out_r, in_r, in_b = lists(k)
+        rows = pool.view(rows_total, comp)
+        ro = torch.tensor(out_r)
+        got = rows[ro].to(dev).view(n, sh.num_segments, sh.page_bytes)
+        ob = torch.tensor(out_b, device=dev)
+        ib = torch.tensor(in_b, device=dev)
+        ri = rows[torch.tensor(in_r)].to(dev).view(n, sh.num_segments, sh.page_bytes)
+        for si, p in enumerate(pages):
+            pv = p.view(-1, sh.page_bytes)
+            if not torch.equal(got[:, si], pv[ob]) or not torch.equal(ri[:, si], pv[ib]):
+                return False
+        return True
+
+    per_step = 2 * n * comp
+    out = {}
+    for m_out, m_in in (("auto", "auto"), ("sm", "sm"), ("ce", "ce"), ("ce", "sm"),
+                        ("sm", "ce")):
+        for k in range(args.warmup):
+            step(k, m_out, m_in)
+        torch.cuda.synchronize()
+        cur = torch.cuda.current_stream(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(cur)
+        sw.swap_out_stream.wait_event(a)
+        sw.swap_in_stream.wait_event(a)
+        for k in range(args.steps):
+            used = step(args.warmup + k, m_out, m_in)
+        cur.wait_stream(sw.swap_out_stream)
+        cur.wait_stream(sw.swap_in_stream)
+        b.record(cur)
+        b.synchronize()
+        t = a.elapsed_time(b) / 1e3
+        gbs = per_step * args.steps / t / 1e9
+        out[f"{m_out}/{m_in}"] = {"gbs": round(gbs, 2), "frac": round(gbs / peaks["bidir_gbs"], 3),
+                                  "modes_used": "/".join(used),
+                                  "bit_exact": check(args.warmup + args.steps - 1)}
+    sw.close()
+    best = max(out, key=lambda k: out[k]["gbs"])
+    return {"impl": args.impl, "metric": METRIC, "value": out["auto/auto"]["gbs"], "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "dtype": "u8", "data": "synthetic, seeded",
+            "config": {"workload": "fragmented host slots, both directions: Qwen2.5-7B-shaped "
+                                   f"cache ({sh.num_segments} x 16 KiB pages, {comp} B host rows), "
+                                   f"{n} blocks out to shuffled rows and {n} in from other "
+                                   f"shuffled rows of a {rows_total}-row pool per step"},
+            "bidir_peak_gbs": peaks["bidir_gbs"], "best": best, "modes": out}
+
+
 SMALL_CALL_BLOCKS = (1, 2, 4, 16, 64, 256)
 
 
@@ -2061,7 +2166,7 @@ def main():
     args = parse_args()
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
-        if args.config in (1, 4, 5, 7) and rank != 0:
+        if args.config in (1, 4, 5, 7, 9) and rank != 0:
             return
         if args.config == 3:
             if args.impl != "reference":
@@ -2078,7 +2183,8 @@ def main():
             if rank == 0:
                 emit(run_config6(args))
             return
-        fn = {1: run_config1, 4: run_config4, 5: run_config5, 7: run_config7}[args.config]
+        fn = {1: run_config1, 4: run_config4, 5: run_config5, 7: run_config7,
+              9: run_config9}[args.config]
         line = fn(args)
         if line is not None:
             emit(line)
