@@ -101,6 +101,7 @@ SIGNATURES = {
     "kvx_device_status": (_int, [_int, _int, ctypes.POINTER(_int)]),
     "kvx_selftest_bounded_wait": (_int, [_u64, _vp]),
     "kvx_configure": (_int, [_i64, _i64, _i64, _i64, _i64]),
+    "kvx_set_option": (_int, [ctypes.c_char_p, _i64]),
     "kvx_swap_noalloc": (_int, [_p_i64, _p_i64, _i64, _int, _vp, _u64, _u64, _vp, _u64, _vp]),
     "kvx_safetensors_meta_json": (_int, [ctypes.c_char_p, ctypes.c_char_p, _u64, _p_u64]),
 }
@@ -245,6 +246,11 @@ def configure(sm_ctas_host: int = 0, sm_ctas_dev: int = 0, ce_min_run: int = 0,
     ce_pipeline: -1 keeps, 0 off, 1 double-buffered staging)."""
     check(lib().kvx_configure(sm_ctas_host, sm_ctas_dev, ce_min_run, staging_bytes,
                               ce_pipeline))
+
+
+def set_option(name: str, value: int) -> None:
+    """Set one tuning knob of the library by name (kvx_set_option)."""
+    check(lib().kvx_set_option(name.encode(), int(value)))
 
 
 def device_status(device: int, reset: bool = False) -> int:

@@ -72,6 +72,8 @@ int from_plan(const Error& e) {
 }
 
 // ---- tunables ----------------------------------------------------------------
+constexpr int kMaxCeStreams = 8;
+
 struct Tunables {
   int64_t sm_ctas_host = 0;    // 0: number of SMs
   int64_t sm_ctas_dev = 0;     // 0: 4 x number of SMs
@@ -88,6 +90,11 @@ struct Tunables {
   int64_t staging_bulk = 1;      // staging gather/scatter: 1 TMA kernel, 0 vector kernel
   int64_t inline_lists = 1;      // small grid plans passed in kernel parameters
   int64_t direct_max = 2;        // AUTO: at most this many copies go straight to the copy engine
+  // Copy-engine mode: the host-run copies of one call spread round-robin over
+  // this many streams (each feeds its own copy-engine queue), so the setup
+  // gap of one short copy overlaps the transfer of another.
+  int64_t ce_streams = 1;
+  int64_t ce_streams_max_run = 4ll << 20;  // ... only when the mean run is at most this
 };
 std::mutex g_tun_mu;
 Tunables g_tun;
@@ -113,6 +120,9 @@ Tunables tunables() {
     g_tun.staging_bulk = env_i64("KVX_STAGING_BULK", g_tun.staging_bulk) ? 1 : 0;
     g_tun.inline_lists = env_i64("KVX_INLINE", g_tun.inline_lists) ? 1 : 0;
     g_tun.direct_max = env_i64("KVX_DIRECT_MAX", g_tun.direct_max);
+    g_tun.ce_streams = std::max<int64_t>(1, std::min<int64_t>(
+        kMaxCeStreams, env_i64("KVX_CE_STREAMS", g_tun.ce_streams)));
+    g_tun.ce_streams_max_run = env_i64("KVX_CE_STREAMS_MAX_RUN", g_tun.ce_streams_max_run);
   });
   std::lock_guard<std::mutex> g(g_tun_mu);
   return g_tun;
@@ -133,6 +143,10 @@ struct Staging {
   // `helper` while the copy engines move the other half on the caller's stream.
   cudaStream_t helper = nullptr;
   cudaEvent_t ev_start = nullptr, ev_dev[2] = {}, ev_link[2] = {};
+  // Streams that share the host-run copies of one call (run_streams > 1).
+  cudaStream_t run_stream[kMaxCeStreams] = {};
+  cudaEvent_t run_done[kMaxCeStreams] = {};
+  cudaEvent_t run_fork = nullptr;
 };
 
 struct DeviceState {
@@ -284,6 +298,16 @@ int pipeline_ready(Staging* sg) {
   for (int b = 0; b < 2; ++b) {
     KVX_CUDA(cudaEventCreateWithFlags(&sg->ev_dev[b], cudaEventDisableTiming));
     KVX_CUDA(cudaEventCreateWithFlags(&sg->ev_link[b], cudaEventDisableTiming));
+  }
+  return KVX_OK;
+}
+
+int run_streams_ready(Staging* sg, int k) {
+  if (!sg->run_fork) KVX_CUDA(cudaEventCreateWithFlags(&sg->run_fork, cudaEventDisableTiming));
+  for (int j = 0; j < k; ++j) {
+    if (sg->run_stream[j]) continue;
+    KVX_CUDA(cudaStreamCreateWithFlags(&sg->run_stream[j], cudaStreamNonBlocking));
+    KVX_CUDA(cudaEventCreateWithFlags(&sg->run_done[j], cudaEventDisableTiming));
   }
   return KVX_OK;
 }
@@ -732,6 +756,49 @@ int run_ce_grid(DeviceState* st, const GridPlan& p, cudaStream_t s, const Tunabl
   size_t off = 0;
   rc = upload(st, up, s, &off);  // the table copy is ordered on s, before ev_start
   if (rc) return rc;
+  // Short host runs: the copies of each chunk go round-robin over k streams
+  // forked from s (and joined back into s), so copy engines overlap their
+  // per-copy gaps.
+  size_t n_runs = 0;
+  for (const auto& rr : runs) n_runs += rr.size();
+  int k_streams = 1;
+  if (!pipelined && tn.ce_streams > 1 && n_runs > 1 &&
+      p.copied / std::max<size_t>(n_runs, 1) <= uint64_t(tn.ce_streams_max_run)) {
+    k_streams = int(std::min<int64_t>(tn.ce_streams, int64_t(n_runs)));
+    rc = run_streams_ready(sg, k_streams);
+    if (rc) return rc;
+  }
+  auto copy_runs = [&](const std::vector<Run>& rr) -> int {
+    if (k_streams == 1) {
+      for (const Run& r : rr) {
+        if (host_is_src)
+          KVX_CUDA(cudaMemcpyAsync(sg->dev + r.staging, reinterpret_cast<const void*>(r.host),
+                                   r.len, cudaMemcpyHostToDevice, s));
+        else
+          KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.host), sg->dev + r.staging, r.len,
+                                   cudaMemcpyDeviceToHost, s));
+      }
+      return KVX_OK;
+    }
+    KVX_CUDA(cudaEventRecord(sg->run_fork, s));
+    for (int j = 0; j < k_streams; ++j)
+      KVX_CUDA(cudaStreamWaitEvent(sg->run_stream[j], sg->run_fork, 0));
+    for (size_t i = 0; i < rr.size(); ++i) {
+      const Run& r = rr[i];
+      cudaStream_t q = sg->run_stream[i % size_t(k_streams)];
+      if (host_is_src)
+        KVX_CUDA(cudaMemcpyAsync(sg->dev + r.staging, reinterpret_cast<const void*>(r.host),
+                                 r.len, cudaMemcpyHostToDevice, q));
+      else
+        KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.host), sg->dev + r.staging, r.len,
+                                 cudaMemcpyDeviceToHost, q));
+    }
+    for (int j = 0; j < k_streams; ++j) {
+      KVX_CUDA(cudaEventRecord(sg->run_done[j], sg->run_stream[j]));
+      KVX_CUDA(cudaStreamWaitEvent(s, sg->run_done[j], 0));
+    }
+    return KVX_OK;
+  };
   cudaStream_t h = pipelined ? sg->helper : s;
   if (pipelined) {
     KVX_CUDA(cudaEventRecord(sg->ev_start, s));
@@ -741,9 +808,8 @@ int run_ce_grid(DeviceState* st, const GridPlan& p, cudaStream_t s, const Tunabl
     const int b = buf_of[i];
     if (host_is_src) {
       if (pipelined && i >= 2) KVX_CUDA(cudaStreamWaitEvent(s, sg->ev_dev[b], 0));
-      for (const Run& r : runs[i])
-        KVX_CUDA(cudaMemcpyAsync(sg->dev + r.staging, reinterpret_cast<const void*>(r.host),
-                                 r.len, cudaMemcpyHostToDevice, s));
+      rc = copy_runs(runs[i]);
+      if (rc) return rc;
       if (pipelined) {
         KVX_CUDA(cudaEventRecord(sg->ev_link[b], s));
         KVX_CUDA(cudaStreamWaitEvent(h, sg->ev_link[b], 0));
@@ -759,9 +825,8 @@ int run_ce_grid(DeviceState* st, const GridPlan& p, cudaStream_t s, const Tunabl
         KVX_CUDA(cudaEventRecord(sg->ev_dev[b], h));
         KVX_CUDA(cudaStreamWaitEvent(s, sg->ev_dev[b], 0));
       }
-      for (const Run& r : runs[i])
-        KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.host), sg->dev + r.staging, r.len,
-                                 cudaMemcpyDeviceToHost, s));
+      rc = copy_runs(runs[i]);
+      if (rc) return rc;
       if (pipelined) KVX_CUDA(cudaEventRecord(sg->ev_link[b], s));
     }
   }
@@ -1152,6 +1217,34 @@ int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev, int64_t ce_min_run,
   if (ce_min_run != 0) g_tun.ce_min_run = ce_min_run < 0 ? 0 : ce_min_run;
   if (staging_bytes > 0) g_tun.staging_bytes = staging_bytes;
   if (ce_pipeline >= 0) g_tun.ce_pipeline = ce_pipeline;
+  return KVX_OK;
+}
+
+int kvx_set_option(const char* name, int64_t value) {
+  t_last_error.clear();
+  if (!name) return set_error(KVX_ERR_INVALID_ARGUMENT, "null option name");
+  tunables();
+  std::lock_guard<std::mutex> g(g_tun_mu);
+  const std::string n(name);
+  if (n == "ce_streams") {
+    if (value < 1 || value > kMaxCeStreams)
+      return set_error(KVX_ERR_INVALID_ARGUMENT, "ce_streams must be in [1, 8]");
+    g_tun.ce_streams = value;
+  } else if (n == "ce_streams_max_run") {
+    g_tun.ce_streams_max_run = value;
+  } else if (n == "ce_min_run") {
+    g_tun.ce_min_run = value < 0 ? 0 : value;
+  } else if (n == "ce_min_bytes") {
+    g_tun.ce_min_bytes = value;
+  } else if (n == "sm_ctas_host") {
+    g_tun.sm_ctas_host = value;
+  } else if (n == "sm_ctas_dev") {
+    g_tun.sm_ctas_dev = value;
+  } else if (n == "direct_max") {
+    g_tun.direct_max = value;
+  } else {
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "unknown option " + n);
+  }
   return KVX_OK;
 }
 

@@ -2042,8 +2042,11 @@ def run_config9(args):
 
     per_step = 2 * n * comp
     out = {}
-    for m_out, m_in in (("auto", "auto"), ("sm", "sm"), ("ce", "ce"), ("ce", "sm"),
-                        ("sm", "ce")):
+    variants = [("auto", "auto", 0), ("sm", "sm", 1), ("ce", "ce", 1), ("ce", "ce", 2),
+                ("ce", "ce", 3), ("ce", "ce", 4), ("ce", "sm", 2), ("sm", "ce", 2)]
+    for m_out, m_in, streams in variants:
+        if streams:
+            _lib.set_option("ce_streams", streams)
         for k in range(args.warmup):
             step(k, m_out, m_in)
         torch.cuda.synchronize()
@@ -2060,9 +2063,10 @@ def run_config9(args):
         b.synchronize()
         t = a.elapsed_time(b) / 1e3
         gbs = per_step * args.steps / t / 1e9
-        out[f"{m_out}/{m_in}"] = {"gbs": round(gbs, 2), "frac": round(gbs / peaks["bidir_gbs"], 3),
-                                  "modes_used": "/".join(used),
-                                  "bit_exact": check(args.warmup + args.steps - 1)}
+        key = f"{m_out}/{m_in}" + (f"/{streams}streams" if streams else "")
+        out[key] = {"gbs": round(gbs, 2), "frac": round(gbs / peaks["bidir_gbs"], 3),
+                    "modes_used": "/".join(used),
+                    "bit_exact": check(args.warmup + args.steps - 1)}
     sw.close()
     best = max(out, key=lambda k: out[k]["gbs"])
     return {"impl": args.impl, "metric": METRIC, "value": out["auto/auto"]["gbs"], "unit": "GB/s",

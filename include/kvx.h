@@ -305,6 +305,15 @@ int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
                   int64_t ce_min_run, int64_t staging_bytes,
                   int64_t ce_pipeline /* -1 keep, 0 off, 1 on */);
 
+/* One tuning knob by name (0 on success, KVX_ERR_INVALID_ARGUMENT for an
+ * unknown name or a value out of range).  Names: "ce_streams" (1..8: streams
+ * that share the host-run copies of one copy-engine call; default 1, env
+ * KVX_CE_STREAMS), "ce_streams_max_run" (those streams are used only when the
+ * mean host run is at most this many bytes; env KVX_CE_STREAMS_MAX_RUN),
+ * "ce_min_run", "ce_min_bytes", "sm_ctas_host", "sm_ctas_dev", "direct_max"
+ * (as above).  Settings are process-wide. */
+int kvx_set_option(const char* name, int64_t value);
+
 /* ---- (f4) safetensors header ------------------------------------------------
  * Reads the header of a .safetensors file and validates it as the
  * `safetensors` crate 0.4.3 does (SafeTensors::read_metadata): header length,
