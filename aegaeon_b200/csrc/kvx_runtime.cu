@@ -77,7 +77,13 @@ constexpr int kMaxCeStreams = 8;
 struct Tunables {
   int64_t sm_ctas_host = 0;    // 0: number of SMs
   int64_t sm_ctas_dev = 0;     // 0: 4 x number of SMs
-  int64_t ce_min_run = 1ll << 20;
+  // Mean coalesced host run from which AUTO stages through the copy engines.
+  // Measured on B200 (896 KiB rows, scattered in groups): the copy engines
+  // pay about 5 us per copy, so with ~1.2 MiB runs they reach 0.81 of the
+  // link one way and 0.67 with both directions active, where the SM path
+  // holds 0.92 and 0.70; from ~2.3 MiB runs the copy engines win with both
+  // directions active (0.75 vs 0.71) and from ~4.7 MiB one way as well.
+  int64_t ce_min_run = 2ll << 20;
   // AUTO stages through the copy engines only from this payload up: below it
   // one zero-copy kernel beats gather + DMA (measured on B200: the SM path is
   // 3-17% faster from 0.5 to 8 MiB per call, the copy engines 3-6% faster at

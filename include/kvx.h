@@ -57,7 +57,7 @@ extern "C" {
 #define KVX_MODE_AUTO 0     /* per-call choice by size and fragmentation:      */
                             /* at most 2 coalesced copies -> CE_EXTENT; host   */
                             /* memory not mapped -> CE; payload >= 16 MiB with */
-                            /* mean host run >= 1 MiB -> CE; otherwise SM       */
+                            /* mean host run >= 2 MiB -> CE; otherwise SM       */
 #define KVX_MODE_SM 1       /* SM kernel, 32-byte vector loads/stores; host    */
                             /* side through its device-mapped address          */
 #define KVX_MODE_CE 2       /* copy engines over coalesced runs; HBM side      */
