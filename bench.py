@@ -1613,6 +1613,10 @@ class Cfg5:
         for k in range(warmup):
             step(k)
         torch.cuda.synchronize()
+        if steps == 0:
+            if impl != "reference":
+                sw.close()
+            return {}
         lat = []
         t0 = time.perf_counter()
         for k in range(steps):
@@ -1737,30 +1741,50 @@ def run_config4(args):
 
 
 def run_config5(args):
-    """Standalone configuration 5 on one GPU, all 24 layers unless the host
-    cannot page-lock 48 GiB (then fewer, stated)."""
+    """Configuration 5 standalone: every rank (torchrun; one GPU alone
+    without it) swaps out its own 16,384-entry fragmented mapping at the same
+    time, either arm.  All 24 layers unless the host cannot page-lock 48 GiB
+    per rank (then fewer, stated).  Box aggregate GB/s over the slowest rank;
+    per-call latency of rank 0; every rank's output checked byte for byte."""
     import torch
 
     from aegaeon_b200 import workloads
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
+    dist_ = Dist.init(use_pg=True)
+    dev = torch.device("cuda", dist_.local_rank)
     layers = 24
     try:
         avail = int([l for l in open("/proc/meminfo")
                      if l.startswith("MemAvailable")][0].split()[1]) * 1024
         per_layer = 2 * 16384 * workloads.CFG5.page_bytes
-        layers = max(1, min(24, int(0.4 * avail // per_layer)))
+        layers = max(1, min(24, int(0.4 * avail / dist_.world // per_layer)))
     except (OSError, IndexError, ValueError):
         pass
-    c = Cfg5(dev, layers=layers)
-    r = c.run(args.impl, args.steps, args.warmup, args.mode,
-              ref=_ref_module() if args.impl == "reference" else None)
-    line = _line_for(args, r, f"cfg5 Qwen1.5-MoE-A2.7B fragmented swap-out: {layers} of 24 "
-                     "layers x K/V 64 KiB pages, 16384 entries (half in contiguous device runs "
-                     "of 1..32 blocks, half isolated), host slots sequential; one call per step",
-                     args.impl, {"call_latency_ms": r["call_ms"]})
-    line["e2e"].update({"h2d_bytes_per_step": 0, "d2h_bytes_per_step": c.call_bytes})
+    layers = int(dist_.max(float(-layers)) * -1)  # the smallest over ranks
+    c = Cfg5(dev, layers=layers, seed=dist_.rank)
+    ref = _ref_module() if args.impl == "reference" else None
+    # warm-up outside the window, then barrier-started timed calls
+    c.run(args.impl, 0, args.warmup, args.mode, ref=ref)
+    dist_.barrier()
+    r = c.run(args.impl, args.steps, 0, args.mode, ref=ref)
+    t = dist_.max(r["seconds"])
+    wall = dist_.max(r["wall"])
+    exact = dist_.gather_obj(r["bit_exact"])
+    c.close()
+    dist_.finish()
+    if dist_.rank != 0:
+        return None
+    total = c.call_bytes * args.steps * dist_.world
+    line = _line_for(args, {"gbs": total / t / 1e9, "seconds": t, "e2e_gbs": total / wall / 1e9,
+                            "bit_exact": all(exact)},
+                     f"cfg5 Qwen1.5-MoE-A2.7B fragmented swap-out: {layers} of 24 layers x K/V "
+                     "64 KiB pages, 16384 entries per GPU (half in contiguous device runs of "
+                     "1..32 blocks, half isolated), host slots sequential; one call per step, "
+                     "every GPU at once", args.impl,
+                     {"n_gpus": dist_.world, "scaling": "weak",
+                      "call_latency_ms_rank0": r["call_ms"]})
+    line["e2e"].update({"h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": c.call_bytes * dist_.world})
     return line
 
 
@@ -2197,7 +2221,7 @@ def main():
     args = parse_args()
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
-        if args.config in (1, 4, 5, 7, 9) and rank != 0:
+        if args.config in (1, 4, 7, 9) and rank != 0:
             return
         if args.config == 3:
             if args.impl != "reference":
