@@ -979,6 +979,7 @@ def run_kvx(args):
     dram = host_dram_copy_gbs() if dist_.rank == 0 else None
     dist_.barrier()
     bench = SwapBench(dev, per_dir, args.cache_blocks)
+    bench.host_peaks = peaks
     lists = [bench.step_lists(k) for k in range(args.warmup + args.steps)]
     for k in range(args.warmup):
         bench.issue(lists[k], args.mode)
@@ -1678,6 +1679,23 @@ def baseline_configs(dev, bench, cfg5_layers: int = 4) -> dict:
     c4.close()
     del c4
     torch.cuda.empty_cache()
+    # scattered host slots, both directions at once (AUTO picks the mode):
+    # the headline 8 MiB rows (the cfg2 cache and pool of the headline run) and
+    # 896 KiB rows (the Qwen2.5-7B shape)
+    bidir = bench.host_peaks["bidir_gbs"]
+    frag = FragSwap(dev, bench.shape, bench.per_dir, bench.rows, bench.pages, bench.pool,
+                    bench.segments, bench.sw)
+    r = frag.run(3, 1, "auto", "auto", group=1)
+    out["frag_8mib_rows"] = {"gbs": round(r["gbs"], 2), "frac_of_bidir_peak": round(r["gbs"] / bidir, 3),
+                             "modes": r["modes_used"], "bit_exact": r["bit_exact"]}
+    frag = FragSwap(dev, workloads.CFG3, 1024, 4096)
+    r = frag.run(3, 1, "auto", "auto", group=1)
+    out["frag_896kib_rows"] = {"gbs": round(r["gbs"], 2),
+                               "frac_of_bidir_peak": round(r["gbs"] / bidir, 3),
+                               "modes": r["modes_used"], "bit_exact": r["bit_exact"]}
+    frag.close()
+    del frag
+    torch.cuda.empty_cache()
     c5 = Cfg5(dev, layers=cfg5_layers)
     pair("cfg5", c5, 3, 1, extra=lambda k, r: {
         "layers": cfg5_layers, "kvx_call_ms": round(statistics.median(k["call_ms"]), 1),
@@ -1687,7 +1705,8 @@ def baseline_configs(dev, bench, cfg5_layers: int = 4) -> dict:
     torch.cuda.empty_cache()
     out["how"] = ("both arms here, same inputs; cfg1 72 tensors x 256 blocks out+in; cfg4 "
                   "2048-block swap-in + 14.17 GB weights; cfg5 16384 fragmented entries, "
-                  f"{cfg5_layers} of 24 layers; outputs compared byte for byte")
+                  f"{cfg5_layers} of 24 layers; frag_*: 1024 blocks out and 1024 in at once "
+                  "over shuffled host rows, AUTO mode; outputs compared byte for byte")
     return out
 
 
@@ -1995,139 +2014,180 @@ def run_config8(args):
     dist_.finish()
 
 
-def run_config9(args):
-    """Fragmented host slots with both directions active.  The reference's
-    CPU slab allocator hands out host slots from a free list
+class FragSwap:
+    """Swap-out and swap-in at once with scattered host slots.  The
+    reference's CPU slab allocator hands out host slots from a free list
     (block_manager.py:942-1031), so after some churn the slots of one swap
-    are scattered rows of the pool.  Workload: a Qwen2.5-7B-shaped cache (28
-    layers x K/V, 16 KiB pages: 896 KiB host rows, below the 1 MiB host run
-    that AUTO needs for the copy engines); per step 1024 random blocks out to 1024
-    shuffled rows of a 4096-row pool and 1024 other blocks in from other
-    shuffled rows, on the two swap streams at once.  Every transfer-mode
-    pair (swap-out mode, swap-in mode) is timed and its last step checked
-    byte for byte; GB/s both directions together against the live
-    bidirectional copy-engine peak."""
-    import torch
+    are scattered rows of the pool.  Per step `n` random blocks go out to `n`
+    rows and `n` other blocks come in from `n` other rows of a `rows_total`-row
+    pool; the rows are shuffled in groups of `group` consecutive rows (host
+    runs of about `group` rows).  The cache and pool may be borrowed (the
+    headline run's), else they are made here for `shape`."""
 
-    from aegaeon_b200 import _lib, swapper, workloads
+    def __init__(self, dev, shape, n: int, rows_total: int, pages=None, pool=None,
+                 segments=None, sw=None):
+        import torch
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    sh = workloads.CFG3
-    n, rows_total = 1024, 4096
-    gen = torch.Generator(device=dev).manual_seed(0)
-    pages = []
-    for _ in range(sh.num_segments):
-        t = torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
-        workloads.fill_segment(t, sh, gen)
-        pages.append(t)
-    segs, comp = swapper.make_segments([((f"l{i}",), sh.num_blocks * sh.page_bytes)
-                                        for i in range(sh.num_segments)], sh.num_blocks)
-    pool = torch.empty(rows_total * comp, dtype=torch.uint8, pin_memory=True)
-    fill = torch.empty(GIB, dtype=torch.uint8, device=dev)
-    for o in range(0, pool.numel(), GIB):
-        fill.random_(0, 256, generator=gen)
-        pool[o:o + GIB].copy_(fill[:pool.numel() - o])
-    del fill
-    sw = swapper.KVSwapper(0, segs, pages, [frozenset({0})] * sh.num_segments, [1], kv_swap=pool)
-    peaks = host_link_peaks(dev)
-    z, one = [0] * n, [1] * n
+        from aegaeon_b200 import swapper, workloads
 
-    layout = {"rows": "shuffled", "group": 1}
+        self.dev, self.sh, self.n, self.rows_total = dev, shape, n, rows_total
+        sh = shape
+        self.own = sw is None
+        if pages is None:
+            gen = torch.Generator(device=dev).manual_seed(0)
+            pages = []
+            for _ in range(sh.num_segments):
+                t = torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
+                workloads.fill_segment(t, sh, gen)
+                pages.append(t)
+            segments, _ = swapper.make_segments(
+                [((f"l{i}",), sh.num_blocks * sh.page_bytes) for i in range(sh.num_segments)],
+                sh.num_blocks)
+            pool = torch.empty(rows_total * sh.composite_bytes, dtype=torch.uint8,
+                               pin_memory=True)
+            fill = torch.empty(GIB, dtype=torch.uint8, device=dev)
+            for o in range(0, pool.numel(), GIB):
+                fill.random_(0, 256, generator=gen)
+                pool[o:o + GIB].copy_(fill[:pool.numel() - o])
+            del fill
+        if sw is None:
+            sw = swapper.KVSwapper(dev.index, segments, pages, [frozenset({0})] * sh.num_segments,
+                                   [1], kv_swap=pool)
+        self.pages, self.pool, self.sw = pages, pool, sw
+        self.comp = sh.composite_bytes
 
-    def lists(k):
-        blocks = workloads.randperm(sh.num_blocks, 900 + k)
-        g = layout["group"]
-        if layout["rows"] == "shuffled":
-            # groups of g consecutive rows in a random order: host runs of g rows
-            order = workloads.randperm(rows_total // g, 500 + k)
-            rows = [q * g + j for q in order for j in range(g)]
+    def lists(self, k: int, group: int, shuffled: bool = True):
+        from aegaeon_b200 import workloads
+
+        n = self.n
+        blocks = workloads.randperm(self.sh.num_blocks, 900 + k)
+        if shuffled:
+            order = workloads.randperm(self.rows_total // group, 500 + k)
+            rows = [q * group + j for q in order for j in range(group)]
         else:
-            rows = list(range(rows_total))
+            rows = list(range(self.rows_total))
         return blocks[:n], rows[:n], rows[n:2 * n], blocks[n:2 * n]
 
-    def step(k, m_out, m_in):
-        out_b, out_r, in_r, in_b = lists(k)
-        mo = mi = "-"
-        e_out = e_in = None
-        if m_out:
-            e_out = sw.swap_blocks([0], out_b, out_r, z, z, one, [None], False, mode=m_out,
-                                   stream=sw.swap_out_stream)
-            mo = _lib.last_mode_name()
-        if m_in:
-            e_in = sw.swap_blocks([1], in_r, in_b, z, z, one, [None], True, mode=m_in,
-                                  stream=sw.swap_in_stream)
-            mi = _lib.last_mode_name()
-        if e_in is not None:
-            sw.swap_out_stream.wait_event(e_in)
-        if e_out is not None:
-            sw.swap_in_stream.wait_event(e_out)
-        return mo, mi
+    def run(self, steps: int, warmup: int, m_out, m_in, group: int = 1,
+            shuffled: bool = True) -> dict:
+        """Times `steps` steps (either direction may be None); returns GB/s
+        of both directions together, the modes AUTO resolved to and whether
+        the last step's host rows and swapped-in blocks are exact."""
+        import torch
 
-    def check(k) -> bool:
-        out_b, out_r, in_r, in_b = lists(k)
-        rows = pool.view(rows_total, comp)
-        ro = torch.tensor(out_r)
-        got = rows[ro].to(dev).view(n, sh.num_segments, sh.page_bytes)
-        ob = torch.tensor(out_b, device=dev)
-        ib = torch.tensor(in_b, device=dev)
-        ri = rows[torch.tensor(in_r)].to(dev).view(n, sh.num_segments, sh.page_bytes)
-        for si, p in enumerate(pages):
-            pv = p.view(-1, sh.page_bytes)
-            if (check_out and not torch.equal(got[:, si], pv[ob])) or \
-                    (check_in and not torch.equal(ri[:, si], pv[ib])):
-                return False
-        return True
+        from aegaeon_b200 import _lib
 
-    per_step = 2 * n * comp
-    out = {}
-    variants = [("shuffled", 1, "auto", "auto", 0)]
-    for g in (1, 2, 4, 8, 32):
-        for m in ("ce", "sm"):
-            variants += [("shuffled", g, m, m, 1), ("shuffled", g, m, None, 1),
-                         ("shuffled", g, None, m, 1)]
-    variants += [("contiguous", 1, "ce", "ce", 1), ("contiguous", 1, "sm", "sm", 1),
-                 ("shuffled", 1, "ce", "ce", 2)]
-    for rows_kind, group, m_out, m_in, streams in variants:
-        layout["rows"], layout["group"] = rows_kind, group
-        check_out, check_in = m_out is not None, m_in is not None
-        if streams:
-            _lib.set_option("ce_streams", streams)
-        for k in range(args.warmup):
-            step(k, m_out, m_in)
+        sw, n = self.sw, self.n
+        z, one = [0] * n, [1] * n
+
+        def step(k):
+            out_b, out_r, in_r, in_b = self.lists(k, group, shuffled)
+            mo = mi = "-"
+            e_out = e_in = None
+            if m_out:
+                e_out = sw.swap_blocks([0], out_b, out_r, z, z, one, [None], False, mode=m_out,
+                                       stream=sw.swap_out_stream)
+                mo = _lib.last_mode_name()
+            if m_in:
+                e_in = sw.swap_blocks([1], in_r, in_b, z, z, one, [None], True, mode=m_in,
+                                      stream=sw.swap_in_stream)
+                mi = _lib.last_mode_name()
+            if e_in is not None:
+                sw.swap_out_stream.wait_event(e_in)
+            if e_out is not None:
+                sw.swap_in_stream.wait_event(e_out)
+            return mo, mi
+
+        for k in range(warmup):
+            step(k)
         torch.cuda.synchronize()
-        cur = torch.cuda.current_stream(dev)
+        cur = torch.cuda.current_stream(self.dev)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(cur)
         sw.swap_out_stream.wait_event(a)
         sw.swap_in_stream.wait_event(a)
-        for k in range(args.steps):
-            used = step(args.warmup + k, m_out, m_in)
+        used = ("-", "-")
+        for k in range(steps):
+            used = step(warmup + k)
         cur.wait_stream(sw.swap_out_stream)
         cur.wait_stream(sw.swap_in_stream)
         b.record(cur)
         b.synchronize()
         t = a.elapsed_time(b) / 1e3
+        moved = n * self.comp * ((1 if m_out else 0) + (1 if m_in else 0))
+        exact = self._check(warmup + steps - 1, group, shuffled, bool(m_out), bool(m_in))
+        return {"gbs": moved * steps / t / 1e9, "modes_used": "/".join(used), "bit_exact": exact}
+
+    def _check(self, k, group, shuffled, check_out, check_in) -> bool:
+        import torch
+
+        sh, n, page = self.sh, self.n, self.sh.page_bytes
+        out_b, out_r, in_r, in_b = self.lists(k, group, shuffled)
+        rows = self.pool.view(self.rows_total, self.comp)
+        ob = torch.tensor(out_b, device=self.dev)
+        ib = torch.tensor(in_b, device=self.dev)
+        for r0 in range(0, n, 256):
+            r1 = min(n, r0 + 256)
+            got = rows[torch.tensor(out_r[r0:r1])].to(self.dev).view(r1 - r0, sh.num_segments, page)
+            src = rows[torch.tensor(in_r[r0:r1])].to(self.dev).view(r1 - r0, sh.num_segments, page)
+            for si, p in enumerate(self.pages):
+                pv = p.view(-1, page)
+                if check_out and not torch.equal(got[:, si], pv[ob[r0:r1]]):
+                    return False
+                if check_in and not torch.equal(src[:, si], pv[ib[r0:r1]]):
+                    return False
+        return True
+
+    def close(self):
+        if self.own:
+            self.sw.close()
+
+
+def run_config9(args):
+    """Fragmented host slots with both directions active, every transfer
+    mode: a Qwen2.5-7B-shaped cache (28 layers x K/V, 16 KiB pages: 896 KiB
+    host rows), 1024 blocks out to shuffled rows and 1024 in from other
+    shuffled rows of a 4096-row pool per step, rows shuffled in groups of g
+    (host runs of about g rows), each direction alone and both at once, and
+    contiguous rows for comparison.  GB/s against the live copy-engine peaks
+    of the same direction(s); every variant's last step checked byte for
+    byte."""
+    import torch
+
+    from aegaeon_b200 import _lib, workloads
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    fs = FragSwap(dev, workloads.CFG3, 1024, 4096)
+    peaks = host_link_peaks(dev)
+    variants = [(True, 1, "auto", "auto", 0)]
+    for g in (1, 2, 4, 8, 32):
+        for m in ("ce", "sm"):
+            variants += [(True, g, m, m, 1), (True, g, m, None, 1), (True, g, None, m, 1)]
+    variants += [(False, 1, "ce", "ce", 1), (False, 1, "sm", "sm", 1), (True, 1, "ce", "ce", 2),
+                 (True, 1, "ce", "sm", 1), (True, 1, "sm", "ce", 1)]
+    out = {}
+    for shuffled, group, m_out, m_in, streams in variants:
+        if streams:
+            _lib.set_option("ce_streams", streams)
+        r = fs.run(args.steps, args.warmup, m_out, m_in, group, shuffled)
         both = m_out is not None and m_in is not None
-        gbs = per_step // (1 if both else 2) * args.steps / t / 1e9
         peak = peaks["bidir_gbs"] if both else (peaks["d2h_gbs"] if m_out else peaks["h2d_gbs"])
-        key = (f"{rows_kind}" + (f"{group}" if rows_kind == "shuffled" else "")
-               + f":{m_out or '-'}/{m_in or '-'}" + (f"/{streams}streams" if streams else ""))
-        out[key] = {"gbs": round(gbs, 2), "frac": round(gbs / peak, 3),
-                    "modes_used": "/".join(used),
-                    "bit_exact": check(args.warmup + args.steps - 1)}
-    sw.close()
-    best = max(out, key=lambda k: out[k]["gbs"])
+        key = (("shuffled" + str(group)) if shuffled else "contiguous") + \
+            f":{m_out or '-'}/{m_in or '-'}" + (f"/{streams}streams" if streams else "")
+        out[key] = {"gbs": round(r["gbs"], 2), "frac": round(r["gbs"] / peak, 3),
+                    "modes_used": r["modes_used"], "bit_exact": r["bit_exact"]}
+    _lib.set_option("ce_streams", 1)
+    fs.close()
     return {"impl": args.impl, "metric": METRIC, "value": out["shuffled1:auto/auto"]["gbs"],
-            "unit": "GB/s",
-            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "dtype": "u8", "data": "synthetic, seeded",
-            "config": {"workload": "fragmented host slots, both directions: Qwen2.5-7B-shaped "
-                                   f"cache ({sh.num_segments} x 16 KiB pages, {comp} B host rows), "
-                                   f"{n} blocks out to shuffled rows and {n} in from other "
-                                   f"shuffled rows of a {rows_total}-row pool per step"},
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "u8", "data": "synthetic, seeded",
+            "config": {"workload": "fragmented host slots: Qwen2.5-7B-shaped cache "
+                                   f"({workloads.CFG3.num_segments} x 16 KiB pages, "
+                                   f"{workloads.CFG3.composite_bytes} B host rows), 1024 blocks "
+                                   "out and 1024 in per step over a 4096-row pool"},
             "bidir_peak_gbs": peaks["bidir_gbs"], "h2d_peak_gbs": peaks["h2d_gbs"],
-            "d2h_peak_gbs": peaks["d2h_gbs"], "best": best, "modes": out}
+            "d2h_peak_gbs": peaks["d2h_gbs"], "modes": out}
 
 
 SMALL_CALL_BLOCKS = (1, 2, 4, 16, 64, 256)
