@@ -101,6 +101,9 @@ struct Tunables {
   // gap of one short copy overlaps the transfer of another.
   int64_t ce_streams = 1;
   int64_t ce_streams_max_run = 4ll << 20;  // ... only when the mean run is at most this
+  // Largest single copy-engine copy of the staged mode (0: one copy per host
+  // run, however long); longer runs are issued as pieces of this size.
+  int64_t ce_max_copy = 0;
 };
 std::mutex g_tun_mu;
 Tunables g_tun;
@@ -129,6 +132,7 @@ Tunables tunables() {
     g_tun.ce_streams = std::max<int64_t>(1, std::min<int64_t>(
         kMaxCeStreams, env_i64("KVX_CE_STREAMS", g_tun.ce_streams)));
     g_tun.ce_streams_max_run = env_i64("KVX_CE_STREAMS_MAX_RUN", g_tun.ce_streams_max_run);
+    g_tun.ce_max_copy = env_i64("KVX_CE_MAX_COPY", g_tun.ce_max_copy);
   });
   std::lock_guard<std::mutex> g(g_tun_mu);
   return g_tun;
@@ -774,15 +778,20 @@ int run_ce_grid(DeviceState* st, const GridPlan& p, cudaStream_t s, const Tunabl
     rc = run_streams_ready(sg, k_streams);
     if (rc) return rc;
   }
+  const uint64_t piece = tn.ce_max_copy > 0 ? uint64_t(tn.ce_max_copy) : ~uint64_t(0);
   auto copy_runs = [&](const std::vector<Run>& rr) -> int {
     if (k_streams == 1) {
       for (const Run& r : rr) {
-        if (host_is_src)
-          KVX_CUDA(cudaMemcpyAsync(sg->dev + r.staging, reinterpret_cast<const void*>(r.host),
-                                   r.len, cudaMemcpyHostToDevice, s));
-        else
-          KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.host), sg->dev + r.staging, r.len,
-                                   cudaMemcpyDeviceToHost, s));
+        for (uint64_t o = 0; o < r.len; o += piece) {
+          const uint64_t len = std::min(piece, r.len - o);
+          if (host_is_src)
+            KVX_CUDA(cudaMemcpyAsync(sg->dev + r.staging + o,
+                                     reinterpret_cast<const void*>(r.host + o), len,
+                                     cudaMemcpyHostToDevice, s));
+          else
+            KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(r.host + o),
+                                     sg->dev + r.staging + o, len, cudaMemcpyDeviceToHost, s));
+        }
       }
       return KVX_OK;
     }
@@ -1236,6 +1245,9 @@ int kvx_set_option(const char* name, int64_t value) {
     if (value < 1 || value > kMaxCeStreams)
       return set_error(KVX_ERR_INVALID_ARGUMENT, "ce_streams must be in [1, 8]");
     g_tun.ce_streams = value;
+  } else if (n == "ce_max_copy") {
+    if (value < 0) return set_error(KVX_ERR_INVALID_ARGUMENT, "ce_max_copy must be >= 0");
+    g_tun.ce_max_copy = value;
   } else if (n == "ce_streams_max_run") {
     g_tun.ce_streams_max_run = value;
   } else if (n == "ce_min_run") {

@@ -70,11 +70,11 @@ def parse_args():
                         "restatement of Worker.swap_blocks' hot loop (worker.py:2270-2329: "
                         "one torch copy_ per segment and block into composite host rows), "
                         "which cannot run as-is without Ray and vLLM")
-    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8, 9], default=2,
+    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8, 9, 10], default=2,
                    help="BASELINE.json configuration (2 = the headline line; 3 is the "
                         "migration object of the N>=2 line; 7 = latency of small swap calls; "
                         "8 = migration transfer forms at N>=2; 9 = fragmented host slots, both "
-                        "directions)")
+                        "directions; 10 = copy-engine piece size on the headline step)")
     p.add_argument("--mode", default="auto", help="transfer mode: auto|sm|ce|ce_extent")
     p.add_argument("--blocks", type=int, default=1024, help="blocks per direction per step")
     p.add_argument("--cache-blocks", type=int, default=4096,
@@ -2190,6 +2190,41 @@ def run_config9(args):
             "d2h_peak_gbs": peaks["d2h_gbs"], "modes": out}
 
 
+def run_config10(args):
+    """The headline configuration-2 step with the staged copy-engine copies
+    cut into pieces of at most P bytes (`ce_max_copy`), for several P: GB/s
+    of both directions together against the live bidirectional link peak.
+    Single multi-GiB copies run slower than 256 MiB pieces when both
+    directions are active."""
+    import torch
+
+    from aegaeon_b200 import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    per_dir = blocks_per_direction(args.blocks, 1, args.cache_blocks)
+    peaks = host_link_peaks(dev)
+    bench = SwapBench(dev, per_dir, args.cache_blocks)
+    lists = [bench.step_lists(k) for k in range(args.warmup + args.steps)]
+    out = {}
+    for piece_mib in (0, 1024, 512, 256, 128, 64, 0):
+        _lib.set_option("ce_max_copy", piece_mib << 20)
+        for k in range(args.warmup):
+            bench.issue(lists[k], args.mode)
+        torch.cuda.synchronize()
+        t = bench.timed_device(args.steps, args.mode, lambda k: lists[args.warmup + k])
+        gbs = bench.bytes_per_step * args.steps / t / 1e9
+        key = f"{piece_mib}MiB" if piece_mib else "unlimited"
+        out.setdefault(key, []).append(round(gbs, 2))
+    _lib.set_option("ce_max_copy", 0)
+    bench.close()
+    return {"impl": args.impl, "metric": METRIC, "value": max(max(v) for v in out.values()),
+            "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "dtype": "u8",
+            "config": cfg2_config(per_dir, args.cache_blocks, 1),
+            "bidir_peak_gbs": peaks["bidir_gbs"], "gbs_by_piece": out}
+
+
 SMALL_CALL_BLOCKS = (1, 2, 4, 16, 64, 256)
 
 
@@ -2281,7 +2316,7 @@ def main():
     args = parse_args()
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
-        if args.config in (1, 4, 7, 9) and rank != 0:
+        if args.config in (1, 4, 7, 9, 10) and rank != 0:
             return
         if args.config == 3:
             if args.impl != "reference":
@@ -2299,7 +2334,7 @@ def main():
                 emit(run_config6(args))
             return
         fn = {1: run_config1, 4: run_config4, 5: run_config5, 7: run_config7,
-              9: run_config9}[args.config]
+              9: run_config9, 10: run_config10}[args.config]
         line = fn(args)
         if line is not None:
             emit(line)

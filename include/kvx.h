@@ -310,6 +310,8 @@ int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
  * that share the host-run copies of one copy-engine call; default 1, env
  * KVX_CE_STREAMS), "ce_streams_max_run" (those streams are used only when the
  * mean host run is at most this many bytes; env KVX_CE_STREAMS_MAX_RUN),
+ * "ce_max_copy" (largest single copy-engine copy of the staged mode; longer
+ * host runs go as pieces of this size; 0 = no limit, env KVX_CE_MAX_COPY),
  * "ce_min_run", "ce_min_bytes", "sm_ctas_host", "sm_ctas_dev", "direct_max"
  * (as above).  Settings are process-wide. */
 int kvx_set_option(const char* name, int64_t value);
