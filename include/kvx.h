@@ -305,7 +305,8 @@ int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
                   int64_t ce_min_run, int64_t staging_bytes,
                   int64_t ce_pipeline /* -1 keep, 0 off, 1 on */);
 
-/* One tuning knob by name (0 on success, KVX_ERR_INVALID_ARGUMENT for an
+/* No counterpart in the reference (it has no tuning knobs on this path).
+ * One tuning knob by name (0 on success, KVX_ERR_INVALID_ARGUMENT for an
  * unknown name or a value out of range).  Names: "ce_streams" (1..8: streams
  * that share the host-run copies of one copy-engine call; default 1, env
  * KVX_CE_STREAMS), "ce_streams_max_run" (those streams are used only when the
