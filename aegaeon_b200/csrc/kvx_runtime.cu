@@ -1245,6 +1245,16 @@ int kvx_set_option(const char* name, int64_t value) {
     if (value < 1 || value > kMaxCeStreams)
       return set_error(KVX_ERR_INVALID_ARGUMENT, "ce_streams must be in [1, 8]");
     g_tun.ce_streams = value;
+  } else if (n == "staging_bulk") {
+    g_tun.staging_bulk = value ? 1 : 0;
+  } else if (n == "bulk_ctas_per_sm") {
+    if (value != 1 && value != 2)
+      return set_error(KVX_ERR_INVALID_ARGUMENT, "bulk_ctas_per_sm must be 1 or 2");
+    g_tun.bulk_ctas_per_sm = value;
+  } else if (n == "vec_bytes") {
+    if (value != 16 && value != 32)
+      return set_error(KVX_ERR_INVALID_ARGUMENT, "vec_bytes must be 16 or 32");
+    g_tun.vec_bytes = value;
   } else if (n == "ce_max_copy") {
     if (value < 0) return set_error(KVX_ERR_INVALID_ARGUMENT, "ce_max_copy must be >= 0");
     g_tun.ce_max_copy = value;

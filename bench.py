@@ -2191,11 +2191,12 @@ def run_config9(args):
 
 
 def run_config10(args):
-    """The headline configuration-2 step with the staged copy-engine copies
-    cut into pieces of at most P bytes (`ce_max_copy`), for several P: GB/s
-    of both directions together against the live bidirectional link peak.
-    Single multi-GiB copies run slower than 256 MiB pieces when both
-    directions are active."""
+    """The headline configuration-2 step under the copy-engine mode's knobs:
+    the staged copies cut into pieces of at most P bytes (`ce_max_copy`), and
+    the staging gather/scatter kernel (TMA bulk at 1 or 2 CTAs per SM, or the
+    vector kernel at several CTA counts).  Per variant: GB/s of both
+    directions together, and the live gather/scatter kernel's fraction of
+    the HBM peak (mean launch, and over the union of launch intervals)."""
     import torch
 
     from aegaeon_b200 import _lib
@@ -2206,23 +2207,50 @@ def run_config10(args):
     peaks = host_link_peaks(dev)
     bench = SwapBench(dev, per_dir, args.cache_blocks)
     lists = [bench.step_lists(k) for k in range(args.warmup + args.steps)]
-    out = {}
-    for piece_mib in (0, 1024, 512, 256, 128, 64, 0):
-        _lib.set_option("ce_max_copy", piece_mib << 20)
+    hbm = measured_peaks().get("hbm_gbs", 6650.0)
+
+    def timed(tag, out):
         for k in range(args.warmup):
             bench.issue(lists[k], args.mode)
         torch.cuda.synchronize()
+        _lib.kernel_timing_read()
+        _lib.kernel_timing(True)
         t = bench.timed_device(args.steps, args.mode, lambda k: lists[args.warmup + k])
-        gbs = bench.bytes_per_step * args.steps / t / 1e9
-        key = f"{piece_mib}MiB" if piece_mib else "unlimited"
-        out.setdefault(key, []).append(round(gbs, 2))
+        _lib.kernel_timing(False)
+        n_l, ms, busy, nbytes = _lib.kernel_timing_read()
+        out.setdefault(tag, []).append({
+            "gbs": round(bench.bytes_per_step * args.steps / t / 1e9, 2),
+            "kernel_frac": round(nbytes / (ms / 1e3) / 1e9 / hbm, 3) if ms else None,
+            "kernel_frac_union": round(nbytes / (busy / 1e3) / 1e9 / hbm, 3) if busy else None,
+            "launches": n_l})
+
+    pieces = {}
+    for piece_mib in (0, 1024, 256, 64, 0):
+        _lib.set_option("ce_max_copy", piece_mib << 20)
+        timed(f"{piece_mib}MiB" if piece_mib else "unlimited", pieces)
     _lib.set_option("ce_max_copy", 0)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    kernels = {}
+    for tag, opts in (("bulk_2perSM", {"staging_bulk": 1, "bulk_ctas_per_sm": 2}),
+                      ("bulk_1perSM", {"staging_bulk": 1, "bulk_ctas_per_sm": 1}),
+                      ("vec32_592ctas", {"staging_bulk": 0, "sm_ctas_dev": 4 * sms}),
+                      ("vec32_296ctas", {"staging_bulk": 0, "sm_ctas_dev": 2 * sms}),
+                      ("vec32_1184ctas", {"staging_bulk": 0, "sm_ctas_dev": 8 * sms}),
+                      ("bulk_2perSM_again", {"staging_bulk": 1, "bulk_ctas_per_sm": 2})):
+        for k, v in opts.items():
+            _lib.set_option(k, v)
+        timed(tag, kernels)
+    _lib.set_option("staging_bulk", 1)
+    _lib.set_option("bulk_ctas_per_sm", 2)
+    _lib.set_option("sm_ctas_dev", 4 * sms)
     bench.close()
-    return {"impl": args.impl, "metric": METRIC, "value": max(max(v) for v in out.values()),
+    best = max(x["gbs"] for v in list(pieces.values()) + list(kernels.values()) for x in v)
+    return {"impl": args.impl, "metric": METRIC, "value": best,
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "dtype": "u8",
             "config": cfg2_config(per_dir, args.cache_blocks, 1),
-            "bidir_peak_gbs": peaks["bidir_gbs"], "gbs_by_piece": out}
+            "bidir_peak_gbs": peaks["bidir_gbs"], "by_piece": pieces,
+            "by_staging_kernel": kernels}
 
 
 SMALL_CALL_BLOCKS = (1, 2, 4, 16, 64, 256)
