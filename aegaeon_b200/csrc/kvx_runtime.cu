@@ -93,6 +93,7 @@ struct Tunables {
   int64_t ce_pipeline = 0;  // double-buffered staging with a helper stream
   int64_t vec_bytes = 32;   // bytes per thread access of the vector kernel (16 or 32)
   int64_t bulk_ctas_per_sm = 2;  // CTAs per SM of the TMA kernel (1 or 2)
+  int64_t bulk_waves = 1;        // TMA kernel grid = waves x resident CTAs (finer spans)
   int64_t staging_bulk = 1;      // staging gather/scatter: 1 TMA kernel, 0 vector kernel
   int64_t inline_lists = 1;      // small grid plans passed in kernel parameters
   int64_t direct_max = 2;        // AUTO: at most this many copies go straight to the copy engine
@@ -126,6 +127,7 @@ Tunables tunables() {
     g_tun.ce_pipeline = env_i64("KVX_CE_PIPELINE", g_tun.ce_pipeline);
     g_tun.vec_bytes = env_i64("KVX_VEC_BYTES", g_tun.vec_bytes) == 16 ? 16 : 32;
     g_tun.bulk_ctas_per_sm = env_i64("KVX_BULK_CTAS_PER_SM", g_tun.bulk_ctas_per_sm) == 1 ? 1 : 2;
+    g_tun.bulk_waves = std::max<int64_t>(1, env_i64("KVX_BULK_WAVES", g_tun.bulk_waves));
     g_tun.staging_bulk = env_i64("KVX_STAGING_BULK", g_tun.staging_bulk) ? 1 : 0;
     g_tun.inline_lists = env_i64("KVX_INLINE", g_tun.inline_lists) ? 1 : 0;
     g_tun.direct_max = env_i64("KVX_DIRECT_MAX", g_tun.direct_max);
@@ -429,8 +431,8 @@ void launch_list(const List& list, const Launch& l, const DeviceState* st, cudaS
                  const Tunables& tn) {
   if (l.bulk) {
     // Up to two 96 KiB CTAs fit on an SM.
-    const uint32_t grid =
-        std::min<uint32_t>(l.n_tiles, uint32_t(tn.bulk_ctas_per_sm * st->sms));
+    const uint32_t grid = std::min<uint32_t>(
+        l.n_tiles, uint32_t(tn.bulk_ctas_per_sm * st->sms * std::max<int64_t>(tn.bulk_waves, 1)));
     kvx_copy_bulk<List><<<grid, 32, kBulkSmem, s>>>(list, l.n_tiles);
   } else {
     const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(ctas_for(st, l.path, tn)));
@@ -1251,6 +1253,10 @@ int kvx_set_option(const char* name, int64_t value) {
     if (value != 1 && value != 2)
       return set_error(KVX_ERR_INVALID_ARGUMENT, "bulk_ctas_per_sm must be 1 or 2");
     g_tun.bulk_ctas_per_sm = value;
+  } else if (n == "bulk_waves") {
+    if (value < 1 || value > 64)
+      return set_error(KVX_ERR_INVALID_ARGUMENT, "bulk_waves must be in [1, 64]");
+    g_tun.bulk_waves = value;
   } else if (n == "vec_bytes") {
     if (value != 16 && value != 32)
       return set_error(KVX_ERR_INVALID_ARGUMENT, "vec_bytes must be 16 or 32");

@@ -2225,23 +2225,26 @@ def run_config10(args):
             "launches": n_l})
 
     pieces = {}
-    for piece_mib in (0, 1024, 256, 64, 0):
+    for piece_mib in (0, 256):
         _lib.set_option("ce_max_copy", piece_mib << 20)
         timed(f"{piece_mib}MiB" if piece_mib else "unlimited", pieces)
     _lib.set_option("ce_max_copy", 0)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     kernels = {}
     for tag, opts in (("bulk_2perSM", {"staging_bulk": 1, "bulk_ctas_per_sm": 2}),
-                      ("bulk_1perSM", {"staging_bulk": 1, "bulk_ctas_per_sm": 1}),
-                      ("vec32_592ctas", {"staging_bulk": 0, "sm_ctas_dev": 4 * sms}),
-                      ("vec32_296ctas", {"staging_bulk": 0, "sm_ctas_dev": 2 * sms}),
-                      ("vec32_1184ctas", {"staging_bulk": 0, "sm_ctas_dev": 8 * sms}),
-                      ("bulk_2perSM_again", {"staging_bulk": 1, "bulk_ctas_per_sm": 2})):
+                      ("bulk_2perSM_4waves", {"staging_bulk": 1, "bulk_waves": 4}),
+                      ("bulk_2perSM_16waves", {"staging_bulk": 1, "bulk_waves": 16}),
+                      ("vec32_4perSM", {"staging_bulk": 0, "sm_ctas_dev": 4 * sms}),
+                      ("vec32_8perSM", {"staging_bulk": 0, "sm_ctas_dev": 8 * sms}),
+                      ("vec32_16perSM", {"staging_bulk": 0, "sm_ctas_dev": 16 * sms}),
+                      ("vec32_32perSM", {"staging_bulk": 0, "sm_ctas_dev": 32 * sms}),
+                      ("bulk_2perSM_again", {"staging_bulk": 1, "bulk_waves": 1})):
         for k, v in opts.items():
             _lib.set_option(k, v)
         timed(tag, kernels)
     _lib.set_option("staging_bulk", 1)
     _lib.set_option("bulk_ctas_per_sm", 2)
+    _lib.set_option("bulk_waves", 1)
     _lib.set_option("sm_ctas_dev", 4 * sms)
     bench.close()
     best = max(x["gbs"] for v in list(pieces.values()) + list(kernels.values()) for x in v)
