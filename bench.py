@@ -2002,7 +2002,7 @@ def run_config8(args):
         key = (f"{direction}_{mode}" + (f"_{per_sm * sms}ctas" if per_sm else "")
                + (f"_push{frac}" if frac else ""))
         out[key] = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in r.items()}
-    _lib.configure(sm_ctas_dev=4 * sms)
+    _lib.set_option("sm_ctas_dev", 0)  # back to the library default
     if dist_.rank == 0:
         best = max(out, key=lambda k: out[k]["per_pair_gbs"])
         emit({"impl": args.impl, "metric": "P->D migration GB/s per GPU pair (cfg3)",
@@ -2218,11 +2218,15 @@ def run_config10(args):
         t = bench.timed_device(args.steps, args.mode, lambda k: lists[args.warmup + k])
         _lib.kernel_timing(False)
         n_l, ms, busy, nbytes = _lib.kernel_timing_read()
+        iso = bench.kernel_roofline(mode_bulk=bool(_staging_bulk[0]))
         out.setdefault(tag, []).append({
             "gbs": round(bench.bytes_per_step * args.steps / t / 1e9, 2),
             "kernel_frac": round(nbytes / (ms / 1e3) / 1e9 / hbm, 3) if ms else None,
             "kernel_frac_union": round(nbytes / (busy / 1e3) / 1e9 / hbm, 3) if busy else None,
+            "isolated_frac": round(iso["algorithmic_bytes"] / iso["seconds"] / 1e9 / hbm, 3),
             "launches": n_l})
+
+    _staging_bulk = [1]
 
     pieces = {}
     for piece_mib in (0, 256):
@@ -2231,21 +2235,23 @@ def run_config10(args):
     _lib.set_option("ce_max_copy", 0)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
     kernels = {}
-    for tag, opts in (("bulk_2perSM", {"staging_bulk": 1, "bulk_ctas_per_sm": 2}),
-                      ("bulk_2perSM_4waves", {"staging_bulk": 1, "bulk_waves": 4}),
-                      ("bulk_2perSM_16waves", {"staging_bulk": 1, "bulk_waves": 16}),
-                      ("vec32_4perSM", {"staging_bulk": 0, "sm_ctas_dev": 4 * sms}),
-                      ("vec32_8perSM", {"staging_bulk": 0, "sm_ctas_dev": 8 * sms}),
-                      ("vec32_16perSM", {"staging_bulk": 0, "sm_ctas_dev": 16 * sms}),
+    for tag, opts in (("bulk_1wave", {"staging_bulk": 1, "bulk_waves": 1}),
+                      ("bulk_8waves", {"staging_bulk": 1, "bulk_waves": 8}),
+                      ("bulk_16waves", {"staging_bulk": 1, "bulk_waves": 16}),
+                      ("bulk_32waves", {"staging_bulk": 1, "bulk_waves": 32}),
+                      ("bulk_1perSM_16waves", {"staging_bulk": 1, "bulk_ctas_per_sm": 1,
+                                               "bulk_waves": 32}),
                       ("vec32_32perSM", {"staging_bulk": 0, "sm_ctas_dev": 32 * sms}),
-                      ("bulk_2perSM_again", {"staging_bulk": 1, "bulk_waves": 1})):
+                      ("bulk_16waves_again", {"staging_bulk": 1, "bulk_ctas_per_sm": 2,
+                                              "bulk_waves": 16})):
         for k, v in opts.items():
             _lib.set_option(k, v)
+        _staging_bulk[0] = opts["staging_bulk"]
         timed(tag, kernels)
     _lib.set_option("staging_bulk", 1)
     _lib.set_option("bulk_ctas_per_sm", 2)
-    _lib.set_option("bulk_waves", 1)
-    _lib.set_option("sm_ctas_dev", 4 * sms)
+    _lib.set_option("bulk_waves", 16)
+    _lib.set_option("sm_ctas_dev", 0)
     bench.close()
     best = max(x["gbs"] for v in list(pieces.values()) + list(kernels.values()) for x in v)
     return {"impl": args.impl, "metric": METRIC, "value": best,

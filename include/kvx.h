@@ -316,7 +316,8 @@ int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
  * "ce_min_run", "ce_min_bytes", "sm_ctas_host", "sm_ctas_dev", "direct_max",
  * "staging_bulk" (1: TMA bulk kernel for the staging gather/scatter, 0: the
  * vector kernel), "bulk_ctas_per_sm" (1 or 2), "bulk_waves" (1..64: the TMA
- * kernel's grid as this many waves of resident CTAs; env KVX_BULK_WAVES),
+ * kernel's grid as this many waves of resident CTAs, 16 by default; env
+ * KVX_BULK_WAVES),
  * "vec_bytes" (16 or 32), as above.  Settings are process-wide. */
 int kvx_set_option(const char* name, int64_t value);
 
