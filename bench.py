@@ -1989,10 +1989,10 @@ def run_config8(args):
         return
     dev = torch.device("cuda", dist_.local_rank)
     sms = torch.cuda.get_device_properties(dev).multi_processor_count
-    variants = [("pull", "sm", 2, None), ("pull", "sm", 4, None), ("pull", "sm", 16, None),
+    variants = [("pull", "sm", 2, None), ("pull", "sm", 16, None), ("pull", "sm", 32, None),
                 ("pull", "sm_bulk", None, None), ("push", "sm", 2, None),
-                ("push", "sm", 4, None), ("push", "sm_bulk", None, None)]
-    variants += [("split", "sm", 4, f) for f in (0.3, 0.4, 0.5)]
+                ("push", "sm", 16, None), ("push", "sm", 32, None), ("push", "sm_bulk", None, None)]
+    variants += [("split", "sm", 16, f) for f in (0.3, 0.5)]
     out = {}
     for direction, mode, per_sm, frac in variants:
         if per_sm:
