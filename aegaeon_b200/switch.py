@@ -85,7 +85,11 @@ def switch_in(swapper, weights: Sequence[Tuple[torch.Tensor, torch.Tensor]],
     if kv_stream is None:
         kv_stream = swapper.swap_in_stream
     if weight_stream is None:
-        weight_stream = torch.cuda.Stream(torch.device("cuda", swapper.device_index))
+        # one weight stream per swapper, made on first use
+        weight_stream = getattr(swapper, "_weight_stream", None)
+        if weight_stream is None:
+            weight_stream = torch.cuda.Stream(torch.device("cuda", swapper.device_index))
+            swapper._weight_stream = weight_stream
     swapper.swap_blocks(request_ids, source_block_ids, target_block_ids, group_ids,
                         first_kernel_blocks, valid_kernel_blocks, source_events, True,
                         mode=mode, stream=kv_stream)
