@@ -110,6 +110,10 @@ struct Tunables {
   // Largest single copy-engine copy of the staged mode (0: one copy per host
   // run, however long); longer runs are issued as pieces of this size.
   int64_t ce_max_copy = 0;
+  // SM mode with a host side: the TMA bulk kernel (16 KiB bulk copies between
+  // shared memory and the device-mapped host rows) instead of the vector
+  // kernel's 32-byte accesses.  Off by default.
+  int64_t host_bulk = 0;
 };
 std::mutex g_tun_mu;
 Tunables g_tun;
@@ -140,6 +144,7 @@ Tunables tunables() {
         kMaxCeStreams, env_i64("KVX_CE_STREAMS", g_tun.ce_streams)));
     g_tun.ce_streams_max_run = env_i64("KVX_CE_STREAMS_MAX_RUN", g_tun.ce_streams_max_run);
     g_tun.ce_max_copy = env_i64("KVX_CE_MAX_COPY", g_tun.ce_max_copy);
+    g_tun.host_bulk = env_i64("KVX_HOST_BULK", g_tun.host_bulk) ? 1 : 0;
   });
   std::lock_guard<std::mutex> g(g_tun_mu);
   return g_tun;
@@ -600,7 +605,7 @@ int run_sm(DeviceState* st, const std::vector<Copy>& copies,
     std::vector<Copy> w(copies.begin() + begin, copies.begin() + end);
     begin = end;
     coalesce(&w);
-    const bool bulk = allow_bulk && device_side(path) && all_aligned16(w);
+    const bool bulk = allow_bulk && (device_side(path) || tn.host_bulk) && all_aligned16(w);
     int rc = add_items(&up, &launches, w, path, bulk);
     if (rc) return rc;
   }
@@ -612,7 +617,7 @@ int run_sm_grid(DeviceState* st, GridPlan* p, Path path, bool allow_bulk, cudaSt
                 const Tunables& tn) {
   Upload up;
   std::vector<Launch> launches;
-  const bool bulk = allow_bulk && device_side(path) && grid_aligned16(*p);
+  const bool bulk = allow_bulk && (device_side(path) || tn.host_bulk) && grid_aligned16(*p);
   int rc = add_grid(&up, &launches, p, path, bulk);
   if (rc) return rc;
   if (!bulk && tn.inline_lists && fits_inline(*p))
@@ -969,7 +974,8 @@ int execute_host_copies(DeviceState* st, std::vector<Copy>& copies, bool is_swap
                        "needs cudaHostAlloc or cudaHostRegister memory");
     const uint64_t delta = hi.dev_base - host_caller_base;  // modular
     for (Copy& c : copies) (is_swap_in ? c.src : c.dst) += delta;
-    rc = run_sm(st, copies, waves, is_swap_in ? Path::kHostSrc : Path::kHostDst, false, s, tn);
+    rc = run_sm(st, copies, waves, is_swap_in ? Path::kHostSrc : Path::kHostDst,
+                tn.host_bulk != 0, s, tn);
   } else if (mode == KVX_MODE_CE) {
     rc = run_ce_staged(st, copies, waves, is_swap_in, tn.staging_bulk != 0, s, tn);
   } else if (mode == KVX_MODE_CE_EXTENT) {
@@ -1029,7 +1035,8 @@ int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
                        "needs cudaHostAlloc or cudaHostRegister memory");
     const uint64_t delta = hi.dev_base - host_caller_base;  // modular
     for (GridSeg& g : p->segs) (is_swap_in ? g.src_base : g.dst_base) += delta;
-    rc = run_sm_grid(st, p, is_swap_in ? Path::kHostSrc : Path::kHostDst, false, s, tn);
+    rc = run_sm_grid(st, p, is_swap_in ? Path::kHostSrc : Path::kHostDst, tn.host_bulk != 0,
+                     s, tn);
   } else if (mode == KVX_MODE_CE) {
     if (p->row_span && p->row_span <= staging_cap(tn)) {
       rc = run_ce_grid(st, *p, s, tn);
@@ -1252,6 +1259,8 @@ int kvx_set_option(const char* name, int64_t value) {
     if (value < 1 || value > kMaxCeStreams)
       return set_error(KVX_ERR_INVALID_ARGUMENT, "ce_streams must be in [1, 8]");
     g_tun.ce_streams = value;
+  } else if (n == "host_bulk") {
+    g_tun.host_bulk = value ? 1 : 0;
   } else if (n == "staging_bulk") {
     g_tun.staging_bulk = value ? 1 : 0;
   } else if (n == "bulk_ctas_per_sm") {

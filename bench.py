@@ -2069,7 +2069,7 @@ class FragSwap:
         return blocks[:n], rows[:n], rows[n:2 * n], blocks[n:2 * n]
 
     def run(self, steps: int, warmup: int, m_out, m_in, group: int = 1,
-            shuffled: bool = True) -> dict:
+            shuffled: bool = True, host_bulk=(False, False)) -> dict:
         """Times `steps` steps (either direction may be None); returns GB/s
         of both directions together, the modes AUTO resolved to and whether
         the last step's host rows and swapped-in blocks are exact."""
@@ -2085,13 +2085,18 @@ class FragSwap:
             mo = mi = "-"
             e_out = e_in = None
             if m_out:
-                e_out = sw.swap_blocks([0], out_b, out_r, z, z, one, [None], False, mode=m_out,
+                _lib.set_option("host_bulk", int(host_bulk[0]))
+                e_out = sw.swap_blocks([0], out_b, out_r, z, z, one, [None], False,
+                                       mode="sm" if m_out == "smb" else m_out,
                                        stream=sw.swap_out_stream)
-                mo = _lib.last_mode_name()
+                mo = _lib.last_mode_name() + ("+bulk" if host_bulk[0] else "")
             if m_in:
-                e_in = sw.swap_blocks([1], in_r, in_b, z, z, one, [None], True, mode=m_in,
+                _lib.set_option("host_bulk", int(host_bulk[1]))
+                e_in = sw.swap_blocks([1], in_r, in_b, z, z, one, [None], True,
+                                      mode="sm" if m_in == "smb" else m_in,
                                       stream=sw.swap_in_stream)
-                mi = _lib.last_mode_name()
+                mi = _lib.last_mode_name() + ("+bulk" if host_bulk[1] else "")
+            _lib.set_option("host_bulk", 0)
             if e_in is not None:
                 sw.swap_out_stream.wait_event(e_in)
             if e_out is not None:
@@ -2161,16 +2166,22 @@ def run_config9(args):
     fs = FragSwap(dev, workloads.CFG3, 1024, 4096)
     peaks = host_link_peaks(dev)
     variants = [(True, 1, "auto", "auto", 0)]
-    for g in (1, 2, 4, 8, 32):
+    for g in (1, 2, 8):
         for m in ("ce", "sm"):
             variants += [(True, g, m, m, 1), (True, g, m, None, 1), (True, g, None, m, 1)]
-    variants += [(False, 1, "ce", "ce", 1), (False, 1, "sm", "sm", 1), (True, 1, "ce", "ce", 2),
-                 (True, 1, "ce", "sm", 1), (True, 1, "sm", "ce", 1)]
+    variants += [(False, 1, "ce", "ce", 1), (False, 1, "sm", "sm", 1), (True, 1, "ce", "ce", 2)]
+    # SM mode through the TMA bulk kernel (16 KiB bulk copies to / from host rows)
+    variants += [(True, 1, "smb", "smb", 1), (True, 1, "smb", None, 1), (True, 1, None, "smb", 1),
+                 (True, 1, "smb", "sm", 1), (True, 1, "sm", "smb", 1),
+                 (False, 1, "smb", "smb", 1)]
     out = {}
     for shuffled, group, m_out, m_in, streams in variants:
         if streams:
             _lib.set_option("ce_streams", streams)
-        r = fs.run(args.steps, args.warmup, m_out, m_in, group, shuffled)
+        bulk_modes = {"smb"}
+        # "smb": SM mode with host_bulk set for that direction's calls
+        r = fs.run(args.steps, args.warmup, m_out, m_in, group, shuffled,
+                   host_bulk=(m_out in bulk_modes, m_in in bulk_modes))
         both = m_out is not None and m_in is not None
         peak = peaks["bidir_gbs"] if both else (peaks["d2h_gbs"] if m_out else peaks["h2d_gbs"])
         key = (("shuffled" + str(group)) if shuffled else "contiguous") + \

@@ -318,7 +318,10 @@ int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
  * vector kernel), "bulk_ctas_per_sm" (1 or 2), "bulk_waves" (1..64: the TMA
  * kernel's grid as this many waves of resident CTAs, 16 by default; env
  * KVX_BULK_WAVES),
- * "vec_bytes" (16 or 32), as above.  Settings are process-wide. */
+ * "vec_bytes" (16 or 32), "host_bulk" (1: SM-mode copies with a host side
+ * go through the TMA bulk kernel, 16 KiB bulk copies to or from the mapped
+ * host rows; 0 default: the vector kernel; env KVX_HOST_BULK), as above.
+ * Settings are process-wide. */
 int kvx_set_option(const char* name, int64_t value);
 
 /* ---- (f4) safetensors header ------------------------------------------------
