@@ -1640,22 +1640,6 @@ int kvx_ipc_close(int device, void* dev_ptr) {
   return KVX_OK;
 }
 
-int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,
-                       uint64_t chunk_bytes, void* stream) {
-  t_last_error.clear();
-  if (bytes && (!dst_device || !src_host))
-    return set_error(KVX_ERR_INVALID_ARGUMENT, "null pointer");
-  if (chunk_bytes == 0) chunk_bytes = bytes ? bytes : 1;
-  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  for (uint64_t o = 0; o < bytes; o += chunk_bytes) {
-    const uint64_t n = std::min(chunk_bytes, bytes - o);
-    KVX_CUDA(cudaMemcpyAsync(static_cast<char*>(dst_device) + o,
-                             static_cast<const char*>(src_host) + o, n,
-                             cudaMemcpyHostToDevice, s));
-  }
-  return KVX_OK;
-}
-
 int kvx_upload_weights(void* const* dst_device, const void* const* src_host,
                        const uint64_t* bytes, int64_t num_buffers, uint64_t chunk_bytes,
                        int host_threads, void* stream) {
@@ -1712,6 +1696,17 @@ int kvx_upload_weights(void* const* dst_device, const void* const* src_host,
     }
   }
   return KVX_OK;
+}
+
+int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,
+                       uint64_t chunk_bytes, void* stream) {
+  t_last_error.clear();
+  if (bytes && (!dst_device || !src_host))
+    return set_error(KVX_ERR_INVALID_ARGUMENT, "null pointer");
+  if (bytes == 0) return KVX_OK;
+  if (chunk_bytes == 0) chunk_bytes = bytes;
+  const int threads = int(std::max(1u, std::thread::hardware_concurrency()));
+  return kvx_upload_weights(&dst_device, &src_host, &bytes, 1, chunk_bytes, threads, stream);
 }
 
 int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream) {

@@ -190,8 +190,9 @@ int kvx_stream_wait_events(void* stream, kvx_event* const* events, int64_t n);
 int kvx_event_release(kvx_event* event);
 
 /* ---- (f1) chunked weight upload for a model switch --------------------------
- * Host -> device copy of `bytes` bytes issued as copy-engine copies of at most
- * chunk_bytes each on `stream` (64 MiB chunks in the switch pipeline).
+ * Host -> device copy of `bytes` bytes in pieces of at most chunk_bytes on
+ * `stream` (0: one piece): kvx_upload_weights below with one buffer and every
+ * host thread, so a pageable source goes through the bounce buffers.
  * Replaces: the slice_storage.copy_(non_blocking=True) loop,
  * aegaeon/loader/quick_loader.py:398-444.                                    */
 int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,

@@ -77,12 +77,14 @@ def test_chunked_upload_parity(cuda):
     from aegaeon_b200 import _lib
 
     n = (3 << 20) + 12345
-    host = torch.randint(0, 255, (n,), dtype=torch.uint8).pin_memory()
+    pageable = torch.randint(0, 255, (n,), dtype=torch.uint8)
     dev = torch.zeros(n, dtype=torch.uint8, device=cuda)
     s = torch.cuda.current_stream()
-    for chunk in (1 << 20, 4096 + 7, n, 0):
-        dev.zero_()
-        _lib.check(_lib.lib().kvx_upload_chunked(dev.data_ptr(), host.data_ptr(), n, chunk,
-                                                 s.cuda_stream))
-        torch.cuda.synchronize()
-        assert torch.equal(dev.cpu(), host)
+    # page-locked: queued copies; pageable: through the library's bounce buffers
+    for host in (pageable.pin_memory(), pageable):
+        for chunk in (1 << 20, 4096 + 7, n, 0):
+            dev.zero_()
+            _lib.check(_lib.lib().kvx_upload_chunked(dev.data_ptr(), host.data_ptr(), n, chunk,
+                                                     s.cuda_stream))
+            torch.cuda.synchronize()
+            assert torch.equal(dev.cpu(), host)
