@@ -1668,18 +1668,22 @@ int kvx_upload_weights(void* const* dst_device, const void* const* src_host,
     int rc = get_state(device, &st);
     if (rc) return rc;
   }
+  // Pageable pieces go through page-locked bounce buffers of at most 64 MiB
+  // each (the reference's cut size), whatever chunk_bytes asks for.
+  const uint64_t bounce_piece = std::min<uint64_t>(chunk_bytes, uint64_t(64) << 20);
   std::unique_lock<std::mutex> lock;
   if (st) {
     lock = std::unique_lock<std::mutex>(st->upload_mu);
-    int rc = bounce_ready(st, size_t(chunk_bytes));
+    int rc = bounce_ready(st, size_t(bounce_piece));
     if (rc) return rc;
   }
   int next = 0;  // bounce buffer of the next pageable chunk
   for (int64_t i = 0; i < num_buffers; ++i) {
     char* dst = static_cast<char*>(dst_device[i]);
     const char* src = static_cast<const char*>(src_host[i]);
-    for (uint64_t o = 0; o < bytes[i]; o += chunk_bytes) {
-      const uint64_t n = std::min(chunk_bytes, bytes[i] - o);
+    const uint64_t step = pinned[size_t(i)] ? chunk_bytes : bounce_piece;
+    for (uint64_t o = 0; o < bytes[i]; o += step) {
+      const uint64_t n = std::min(step, bytes[i] - o);
       if (pinned[size_t(i)]) {
         KVX_CUDA(cudaMemcpyAsync(dst + o, src + o, n, cudaMemcpyHostToDevice, s));
         continue;

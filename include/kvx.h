@@ -203,8 +203,8 @@ int kvx_upload_chunked(void* dst_device, const void* src_host, uint64_t bytes,
  * the current device in pieces of chunk_bytes, in order, on `stream`.
  *  * Page-locked (or managed) sources: one cudaMemcpyAsync per piece; the
  *    call returns once they are queued.
- *  * Pageable sources: through two page-locked bounce buffers of chunk_bytes
- *    owned by the library (allocated on first use).  host_threads threads copy
+ *  * Pageable sources: through two page-locked bounce buffers of
+ *    min(chunk_bytes, 64 MiB) owned by the library (allocated on first use).  host_threads threads copy
  *    piece k+1 into one bounce buffer while the copy engine moves piece k out
  *    of the other, the two-stage pipeline of the reference's
  *    pipeline_storage_transfer (pageable -> pinned -> device, cut into
