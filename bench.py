@@ -70,11 +70,12 @@ def parse_args():
                         "restatement of Worker.swap_blocks' hot loop (worker.py:2270-2329: "
                         "one torch copy_ per segment and block into composite host rows), "
                         "which cannot run as-is without Ray and vLLM")
-    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8, 9, 10], default=2,
+    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11], default=2,
                    help="BASELINE.json configuration (2 = the headline line; 3 is the "
                         "migration object of the N>=2 line; 7 = latency of small swap calls; "
                         "8 = migration transfer forms at N>=2; 9 = fragmented host slots, both "
-                        "directions; 10 = copy-engine piece size on the headline step)")
+                        "directions; 10 = copy-engine knobs on the headline step; 11 = weight "
+                        "upload from pageable memory, both arms)")
     p.add_argument("--mode", default="auto", help="transfer mode: auto|sm|ce|ce_extent")
     p.add_argument("--blocks", type=int, default=1024, help="blocks per direction per step")
     p.add_argument("--cache-blocks", type=int, default=4096,
@@ -2273,6 +2274,84 @@ def run_config10(args):
             "by_staging_kernel": kernels}
 
 
+def run_config11(args):
+    """Weight upload of a model switch from pageable host memory: the
+    Qwen1.5-14B TP-2 shard (14.17 GB bf16) as four safetensors-sized
+    storages in ordinary (pageable) host memory, uploaded to the GPU.  Both
+    arms run here on the same bytes and are checked byte for byte:
+    * kvx: switch.upload_weights (kvx_upload_weights: 64 MiB pieces through
+      two page-locked bounce buffers, host threads filling one while the
+      copy engine drains the other);
+    * reference: pipeline_storage_transfer restated
+      (quick_model_loader/quick_model_loader/model_loader.py:348-369): per
+      storage a page-locked buffer of its size (allocated once, before the
+      timing, as the loader's pinned allocator does), 16 cuts, each copied
+      host -> page-locked, then the stream synchronized, then copied to the
+      device non-blocking; one final synchronize.
+    Wall-clock GB/s (the host copies are part of the work)."""
+    import torch
+
+    from aegaeon_b200 import switch, workloads
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    torch.set_num_threads(len(os.sched_getaffinity(0)))
+    ws = workloads.WeightShard()
+    cut = -(-ws.nbytes // 4)
+    sizes = [min(cut, ws.nbytes - o) for o in range(0, ws.nbytes, cut)]
+    gen = torch.Generator().manual_seed(11)
+    hosts = [torch.randint(0, 256, (n,), dtype=torch.uint8, generator=gen) for n in sizes]
+    devs = [torch.empty(n, dtype=torch.uint8, device=dev) for n in sizes]
+    stream = torch.cuda.Stream(dev)
+    pinned = [torch.empty(n, dtype=torch.uint8, pin_memory=True) for n in sizes]
+
+    def kvx_once():
+        switch.upload_weights(list(zip(devs, hosts)), chunk_bytes=64 << 20, stream=stream)
+        stream.synchronize()
+
+    def create_cuts(size, cuts_num):
+        base, extra = divmod(size, cuts_num)
+        out, start = [], 0
+        for i in range(cuts_num):
+            end = start + base + (1 if i < extra else 0)
+            out.append((start, end))
+            start = end
+        return out
+
+    def ref_once():
+        with torch.cuda.stream(stream):
+            for d, h, pb in zip(devs, hosts, pinned):
+                size = h.numel()
+                for a, b in create_cuts(size, 1 if size <= GIB else 16):
+                    pb[a:b].copy_(h[a:b], non_blocking=True)
+                    stream.synchronize()
+                    d[a:b].copy_(pb[a:b], non_blocking=True)
+            stream.synchronize()
+
+    out = {}
+    for name, fn in (("kvx", kvx_once), ("reference", ref_once)):
+        for d in devs:
+            d.zero_()
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            fn()
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            fn()
+            times.append(time.perf_counter() - t0)
+        exact = all(torch.equal(d.cpu(), h) for d, h in zip(devs, hosts))
+        t = statistics.median(times)
+        out[name] = {"seconds": round(t, 4), "gbs": round(ws.nbytes / t / 1e9, 2),
+                     "bit_exact": exact}
+    return {"impl": "kvx+reference", "metric": METRIC, "value": out["kvx"]["gbs"], "unit": "GB/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "dtype": "u8", "data": "synthetic, seeded",
+            "config": {"workload": f"Qwen1.5-14B TP-2 shard ({ws.nbytes} B) as 4 pageable "
+                                   "storages uploaded to the GPU"},
+            "arms": out, "ratio": round(out["kvx"]["gbs"] / out["reference"]["gbs"], 2)}
+
+
 SMALL_CALL_BLOCKS = (1, 2, 4, 16, 64, 256)
 
 
@@ -2364,7 +2443,7 @@ def main():
     args = parse_args()
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
-        if args.config in (1, 4, 7, 9, 10) and rank != 0:
+        if args.config in (1, 4, 7, 9, 10, 11) and rank != 0:
             return
         if args.config == 3:
             if args.impl != "reference":
@@ -2382,7 +2461,7 @@ def main():
                 emit(run_config6(args))
             return
         fn = {1: run_config1, 4: run_config4, 5: run_config5, 7: run_config7,
-              9: run_config9, 10: run_config10}[args.config]
+              9: run_config9, 10: run_config10, 11: run_config11}[args.config]
         line = fn(args)
         if line is not None:
             emit(line)
