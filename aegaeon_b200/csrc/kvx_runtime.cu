@@ -16,6 +16,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <condition_variable>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
@@ -1058,24 +1059,99 @@ int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
 
 // ---- weight upload (model switch) ------------------------------------------
 
-// memcpy split over `threads` host threads (the calling thread takes a share).
+// Persistent host threads for the pageable-upload copies: each call splits
+// one memcpy into shares of at least 4 MiB that the pool's threads and the
+// calling thread take in turn; the call returns when every share is copied.
+// One job at a time (uploads of a device already serialize on its bounce
+// buffers).  The pool is created on first use and lives until the process
+// exits.
+class CopyPool {
+ public:
+  static CopyPool& get() {
+    static CopyPool* pool = new CopyPool();  // never destroyed: its threads outlive callers
+    return *pool;
+  }
+
+  void copy(char* dst, const char* src, size_t n, int threads) {
+    constexpr size_t kMinShare = size_t(4) << 20;
+    const size_t parts = std::max<size_t>(
+        1, std::min<size_t>(size_t(std::max(threads, 1)), n / kMinShare));
+    if (parts == 1) {
+      std::memcpy(dst, src, n);
+      return;
+    }
+    std::lock_guard<std::mutex> one_job(call_mu_);
+    grow(int(parts) - 1);
+    auto job = std::make_shared<Job>();
+    job->dst = dst;
+    job->src = src;
+    job->n = n;
+    job->parts = parts;
+    job->share = (n / parts + 4095) & ~size_t(4095);
+    job->left.store(parts);
+    {
+      std::lock_guard<std::mutex> g(mu_);
+      current_ = job;
+      ++generation_;
+    }
+    cv_.notify_all();
+    work(*job);
+    std::unique_lock<std::mutex> g(job->mu);
+    job->done_cv.wait(g, [&] { return job->left.load() == 0; });
+  }
+
+ private:
+  struct Job {
+    char* dst = nullptr;
+    const char* src = nullptr;
+    size_t n = 0, parts = 0, share = 0;
+    std::atomic<size_t> next{0};
+    std::atomic<size_t> left{0};
+    std::mutex mu;
+    std::condition_variable done_cv;
+  };
+
+  static void work(Job& job) {
+    for (;;) {
+      const size_t k = job.next.fetch_add(1);
+      if (k >= job.parts) return;
+      const size_t a = std::min(job.n, k * job.share);
+      const size_t b = k + 1 == job.parts ? job.n : std::min(job.n, (k + 1) * job.share);
+      if (a < b) std::memcpy(job.dst + a, job.src + a, b - a);
+      if (job.left.fetch_sub(1) == 1) {
+        std::lock_guard<std::mutex> g(job.mu);
+        job.done_cv.notify_all();
+      }
+    }
+  }
+
+  void grow(int want) {
+    while (int(workers_.size()) < want) {
+      workers_.emplace_back([this] {
+        uint64_t seen = 0;
+        for (;;) {
+          std::shared_ptr<Job> job;
+          {
+            std::unique_lock<std::mutex> g(mu_);
+            cv_.wait(g, [&] { return generation_ != seen; });
+            seen = generation_;
+            job = current_;
+          }
+          if (job) work(*job);
+        }
+      });
+    }
+  }
+
+  std::mutex call_mu_, mu_;
+  std::condition_variable cv_;
+  std::vector<std::thread> workers_;
+  std::shared_ptr<Job> current_;
+  uint64_t generation_ = 0;
+};
+
 void parallel_memcpy(char* dst, const char* src, size_t n, int threads) {
-  constexpr size_t kMinShare = size_t(4) << 20;
-  threads = int(std::max<size_t>(1, std::min<size_t>(size_t(std::max(threads, 1)),
-                                                      n / kMinShare)));
-  if (threads == 1) {
-    std::memcpy(dst, src, n);
-    return;
-  }
-  const size_t share = (n / threads + 4095) & ~size_t(4095);
-  std::vector<std::thread> pool;
-  pool.reserve(threads - 1);
-  for (int t = 1; t < threads; ++t) {
-    const size_t a = std::min(n, t * share), b = std::min(n, (t + 1) * share);
-    if (a < b) pool.emplace_back([=] { std::memcpy(dst + a, src + a, b - a); });
-  }
-  std::memcpy(dst, src, std::min(n, share));
-  for (std::thread& th : pool) th.join();
+  CopyPool::get().copy(dst, src, n, threads);
 }
 
 int bounce_ready(DeviceState* st, size_t want) {
