@@ -84,6 +84,9 @@ def parse_args():
     p.add_argument("--cpu-seconds", type=float, default=10.0)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-migration", action="store_true")
+    p.add_argument("--set", action="append", default=[], metavar="NAME=VALUE",
+                   help="set a library tuning option (kvx_set_option) before running, e.g. "
+                        "--set sm_ctas_host=296; may repeat")
     p.add_argument("--no-extras", action="store_true",
                    help="N=1: skip the configuration 1/4/5 objects of the default line")
     p.add_argument("--migration-direction", choices=["pull", "push"], default="pull",
@@ -2441,6 +2444,12 @@ def main():
     global _OUT
     _OUT = out
     args = parse_args()
+    if args.set:
+        from aegaeon_b200 import _lib
+
+        for item in args.set:
+            name, _, value = item.partition("=")
+            _lib.set_option(name.strip(), int(value, 0))
     if args.config != 2:
         rank = int(os.environ.get("RANK", "0"))
         if args.config in (1, 4, 7, 9, 10, 11) and rank != 0:
