@@ -193,14 +193,20 @@ struct GridList {
 // A grid list carried in the kernel's parameter space instead of a device
 // table: small requests launch without a descriptor upload.  Entries occupy
 // records [0, n), the segment table records [n, n + n_segs); both are 32-byte
-// records.  Sized so the whole parameter block stays within 4 KiB.
+// records.  Three capacities: 124 records (the parameter block within 4 KiB),
+// 508 (16 KiB) and 1020 (within the 32,764-byte limit that sm_70 and later
+// accept since CUDA 12.1); a launch uses the smallest that holds its plan, so
+// it sends no more parameter bytes than it needs.
 constexpr uint32_t kInlineRecords = 124;
+constexpr uint32_t kInlineRecordsMid = 508;
+constexpr uint32_t kInlineRecordsMax = 1020;
 
-struct InlineGridList {
+template <uint32_t kCap>
+struct InlineGridListT {
   uint32_t n = 0;       // entries
   uint32_t n_segs = 0;  // segments
   uint32_t pad[2] = {};
-  uint4 rec[2 * kInlineRecords];
+  uint4 rec[2 * kCap];
   __host__ __device__ __forceinline__ const GridEntry* entries() const {
     return reinterpret_cast<const GridEntry*>(rec);
   }
@@ -215,7 +221,13 @@ struct InlineGridList {
     grid_resolve(e[cur], segs(), t, shift, src, dst, len);
   }
 };
-static_assert(sizeof(InlineGridList) + 8 <= 4096, "inline list exceeds the parameter limit");
+using InlineGridList = InlineGridListT<kInlineRecords>;
+using InlineGridListMid = InlineGridListT<kInlineRecordsMid>;
+using InlineGridListMax = InlineGridListT<kInlineRecordsMax>;
+// the list plus the kernel's two 32-bit arguments
+static_assert(sizeof(InlineGridList) + 8 <= 4096, "inline list exceeds 4 KiB");
+static_assert(sizeof(InlineGridListMid) + 8 <= 16384, "inline list exceeds 16 KiB");
+static_assert(sizeof(InlineGridListMax) + 8 <= 32764, "inline list exceeds the parameter limit");
 
 template <int kSrc, int kVec, class List>
 __device__ __forceinline__ void copy_tiles(const List& list, uint32_t n_tiles,
@@ -239,10 +251,10 @@ __global__ void __launch_bounds__(kVecThreads)
 }
 
 // Same copy with the work list read in place from the parameter space
-// (__grid_constant__: no per-thread copy of the 4 KiB list).
-template <int kSrc, int kVec>
+// (__grid_constant__: no per-thread copy of the list).
+template <int kSrc, int kVec, class InlineList>
 __global__ void __launch_bounds__(kVecThreads)
-    kvx_copy_vec_inline(const __grid_constant__ InlineGridList list, uint32_t n_tiles,
+    kvx_copy_vec_inline(const __grid_constant__ InlineList list, uint32_t n_tiles,
                         uint32_t tile_shift) {
   copy_tiles<kSrc, kVec>(list, n_tiles, tile_shift);
 }

@@ -502,39 +502,51 @@ int launch_one(DeviceState* st, size_t ring_off, const Launch& l, cudaStream_t s
   return timed(st, l, s, [&] { return launch_kernel(st, ring_off, l, s, tn); });
 }
 
-// Grid plans up to this many records (entries + segments) go to the kernel in
-// its parameters: no descriptor upload, no ring fence.
+// Grid plans up to kInlineRecordsMax records (entries + segments) go to the
+// kernel in its parameters: no descriptor upload, no ring fence.
 bool fits_inline(const GridPlan& p) {
-  return p.entries.size() + p.segs.size() <= kInlineRecords;
+  return p.entries.size() + p.segs.size() <= kInlineRecordsMax;
 }
 
-// One vector-kernel launch of a finalized grid plan passed by value.
-int launch_inline(DeviceState* st, const GridPlan& p, const Launch& l, cudaStream_t s,
-                  const Tunables& tn) {
-  if (l.n_tiles == 0) return KVX_OK;
-  InlineGridList list;
+template <class InlineList>
+int launch_inline_as(const DeviceState* st, const GridPlan& p, const Launch& l, cudaStream_t s,
+                     const Tunables& tn) {
+  InlineList list;
   list.n = uint32_t(p.entries.size());
   list.n_segs = uint32_t(p.segs.size());
   std::memcpy(list.rec, p.entries.data(), p.entries.size() * sizeof(GridEntry));
   std::memcpy(list.rec + 2 * list.n, p.segs.data(), p.segs.size() * sizeof(GridSeg));
   const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(ctas_for(st, l.path, tn)));
   const bool host_src = l.path == Path::kHostSrc;
+  if (tn.vec_bytes == 32) {
+    if (host_src)
+      kvx_copy_vec_inline<kSrcHost, 32, InlineList><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles,
+                                                                                 kVecShift);
+    else
+      kvx_copy_vec_inline<kSrcDevice, 32, InlineList><<<grid, kVecThreads, 0, s>>>(
+          list, l.n_tiles, kVecShift);
+  } else if (host_src) {
+    kvx_copy_vec_inline<kSrcHost, 16, InlineList><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles,
+                                                                               kVecShift);
+  } else {
+    kvx_copy_vec_inline<kSrcDevice, 16, InlineList><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles,
+                                                                                 kVecShift);
+  }
+  KVX_CUDA(cudaGetLastError());
+  g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
+  return KVX_OK;
+}
+
+// One vector-kernel launch of a finalized grid plan passed by value, in the
+// smallest parameter-space list that holds it.
+int launch_inline(DeviceState* st, const GridPlan& p, const Launch& l, cudaStream_t s,
+                  const Tunables& tn) {
+  if (l.n_tiles == 0) return KVX_OK;
+  const size_t records = p.entries.size() + p.segs.size();
   return timed(st, l, s, [&] {
-    if (tn.vec_bytes == 32) {
-      if (host_src)
-        kvx_copy_vec_inline<kSrcHost, 32><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles, kVecShift);
-      else
-        kvx_copy_vec_inline<kSrcDevice, 32><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles,
-                                                                         kVecShift);
-    } else if (host_src) {
-      kvx_copy_vec_inline<kSrcHost, 16><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles, kVecShift);
-    } else {
-      kvx_copy_vec_inline<kSrcDevice, 16><<<grid, kVecThreads, 0, s>>>(list, l.n_tiles,
-                                                                       kVecShift);
-    }
-    KVX_CUDA(cudaGetLastError());
-    g_kernel_launches.fetch_add(1, std::memory_order_relaxed);
-    return KVX_OK;
+    if (records <= kInlineRecords) return launch_inline_as<InlineGridList>(st, p, l, s, tn);
+    if (records <= kInlineRecordsMid) return launch_inline_as<InlineGridListMid>(st, p, l, s, tn);
+    return launch_inline_as<InlineGridListMax>(st, p, l, s, tn);
   });
 }
 

@@ -300,8 +300,9 @@ int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream);
  * KVX_BULK_CTAS_PER_SM (2 default; 1), KVX_CE_MIN_BYTES (16 MiB: smallest
  * payload AUTO stages through the copy engines), KVX_DIRECT_MAX (2: most
  * coalesced copies AUTO sends to the copy engines directly; 0 never) and
- * KVX_INLINE (1: grid plans of at most 124 records travel in the kernel's
- * parameters instead of through the descriptor ring; 0 never). */
+ * KVX_INLINE (1: grid plans of at most 1020 records travel in the kernel's
+ * parameters, in lists of 124, 508 or 1020 records, instead of through the
+ * descriptor ring; 0 never). */
 int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
                   int64_t ce_min_run, int64_t staging_bytes,
                   int64_t ce_pipeline /* -1 keep, 0 off, 1 on */);

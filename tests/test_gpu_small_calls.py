@@ -1,8 +1,9 @@
 """Small requests: the launch forms chosen for them copy the same bytes.
 
-* Grid plans of at most 124 records (entries + segments) reach the vector
-  kernel in its parameters instead of through the descriptor ring; plans on
-  either side of that limit must match the oracle byte for byte.
+* Grid plans of at most 1020 records (entries + segments) reach the vector
+  kernel in its parameters instead of through the descriptor ring, in lists
+  of 124, 508 or 1020 records; plans on either side of each limit must match
+  the oracle byte for byte.
 * In "auto" mode, a request that coalesces into one or two copies goes to the
   copy engine directly ("ce_extent"); one that does not, to the kernel.
 """
@@ -16,6 +17,8 @@ from aegaeon_b200 import _lib, ops, swapper
 pytestmark = pytest.mark.gpu
 
 INLINE_RECORDS = 124
+INLINE_MID = 508
+INLINE_MAX = 1020
 
 
 def make(cuda, nsegs, nb, rows, page, seed):
@@ -29,9 +32,10 @@ def make(cuda, nsegs, nb, rows, page, seed):
     return sw, segs, segments, pool, comp
 
 
-@pytest.mark.parametrize("records", [INLINE_RECORDS - 1, INLINE_RECORDS, INLINE_RECORDS + 1, 300])
+@pytest.mark.parametrize("records", [INLINE_RECORDS - 1, INLINE_RECORDS, INLINE_RECORDS + 1, 300,
+                                     INLINE_MID, INLINE_MID + 1, INLINE_MAX, INLINE_MAX + 1])
 def test_sm_swap_blocks_around_inline_limit(cuda, oracle, records):
-    nsegs, page, nb, rows = 4, 4096, 512, 512
+    nsegs, page, nb, rows = 4, 4096, 1536, 1536
     n = records - nsegs
     sw, segs, segments, pool, comp = make(cuda, nsegs, nb, rows, page, records)
     g = torch.Generator().manual_seed(records)
@@ -56,10 +60,11 @@ def test_sm_swap_blocks_around_inline_limit(cuda, oracle, records):
         sw.close()
 
 
-@pytest.mark.parametrize("n", [INLINE_RECORDS - 1, INLINE_RECORDS, 400])
+@pytest.mark.parametrize("n", [INLINE_RECORDS - 1, INLINE_RECORDS, 400, INLINE_MID,
+                               INLINE_MAX - 1, INLINE_MAX])
 def test_ops_swap_sm_around_inline_limit(cuda, oracle, n):
     """ops.swap plans have one segment: n entries + 1 record."""
-    blocks, slots = 512, 512
+    blocks, slots = 1536, 1536
     g = torch.Generator(device=cuda).manual_seed(n)
     cache = torch.randint(-30000, 30000, (blocks, 1024), dtype=torch.int16, device=cuda,
                           generator=g)
@@ -123,10 +128,11 @@ def test_auto_sends_one_or_two_copies_to_copy_engine(cuda, oracle):
         assert np.array_equal(cache_host, exp_cache)
 
 
-@pytest.mark.parametrize("n", [INLINE_RECORDS - 4, INLINE_RECORDS - 3, 300])
+@pytest.mark.parametrize("n", [INLINE_RECORDS - 4, INLINE_RECORDS - 3, 300, INLINE_MAX - 4,
+                               INLINE_MAX - 3])
 def test_copy_blocks_local_around_inline_limit(cuda, n):
     """On-GPU block copies (migration path, one device): 4 segments."""
-    nsegs, page, nb = 4, 8192, 1024
+    nsegs, page, nb = 4, 8192, 2048
     sw, segs, _, _, _ = make(cuda, nsegs, nb, 8, page, n)
     g = torch.Generator().manual_seed(n)
     ids = torch.randperm(nb, generator=g)[: 2 * n].tolist()
