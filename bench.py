@@ -652,22 +652,34 @@ def _pair_exact(dist_, dev, pages, page: int, ids, is_src: bool, partner: int) -
 
 
 def _peer_copy_peak(dist_, sw, partner: int, direction: str, active: bool, stream, blocks: int,
-                    segments: int, page: int) -> dict:
+                    segments: int, page: int, streams: int = 1) -> dict:
     """Copy-engine peer copy between the pair, same direction and same
     mapped caches as the migration: blocks [0, blocks) of every segment, which
     coalesce into one plain cudaMemcpyAsync per segment (mode ce_extent), in
-    barrier-started windows; best of 5, slowest rank."""
+    barrier-started windows; best of 5, slowest rank.  With streams > 1 the
+    block range is split into that many parts, each on its own stream (each
+    stream may feed another copy engine)."""
     import torch
 
-    ids = list(range(blocks))
+    dev = torch.device("cuda", sw.device_index)
+    parts = [list(range(k * blocks // streams, (k + 1) * blocks // streams))
+             for k in range(streams)]
+    extra = [stream] + [torch.cuda.Stream(dev) for _ in range(streams - 1)]
 
     def run():
-        if active:
+        if not active:
+            return
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        for q, ids in zip(extra, parts):
+            q.wait_event(ev)
             sw.migrate_blocks([0], partner, ids, ids, None, direction=direction,
-                              mode="ce_extent", stream=stream)
+                              mode="ce_extent", stream=q)
+        for q in extra[1:]:
+            stream.wait_stream(q)
 
     run()
-    stream.synchronize()
+    torch.cuda.synchronize(dev)
     nbytes = blocks * segments * page
     best = 0.0
     for _ in range(5):
@@ -1998,6 +2010,33 @@ def run_config8(args):
                 ("push", "sm", 16, None), ("push", "sm", 32, None), ("push", "sm_bulk", None, None)]
     variants += [("split", "sm", 16, f) for f in (0.3, 0.5)]
     out = {}
+    # copy-engine peer copies of contiguous blocks over 1..8 streams, both directions
+    from aegaeon_b200 import swapper, workloads
+
+    sh = workloads.CFG3
+    pages = [torch.empty(sh.num_blocks * sh.page_bytes, dtype=torch.uint8, device=dev)
+             for _ in range(sh.num_segments)]
+    segs, _ = swapper.make_segments([((f"l{i}",), sh.num_blocks * sh.page_bytes)
+                                     for i in range(sh.num_segments)], sh.num_blocks)
+    sw = swapper.KVSwapper(dev.index, segs, pages, [frozenset({0})] * sh.num_segments, [1])
+    handles = dist_.gather_obj(sw.export_kvcache_mem_handles())
+    half = dist_.world // 2
+    is_src = dist_.rank < half
+    partner = dist_.rank + half if is_src else dist_.rank - half
+    sw.register_kvcache_mem_handles(partner, None, handles[partner])
+    st = torch.cuda.Stream(dev)
+    for direction in ("pull", "push"):
+        active = is_src if direction == "push" else not is_src
+        for k in (1, 2, 4, 8):
+            r = _peer_copy_peak(dist_, sw, partner, direction, active, st, 4096,
+                                sh.num_segments, sh.page_bytes, streams=k)
+            out[f"{direction}_copy_engine_{k}streams"] = {
+                "per_pair_gbs": round(r["per_pair_gbs"], 3),
+                "frac_of_nominal_900": round(r["per_pair_gbs"] / 900.0, 3)}
+    dist_.barrier()
+    sw.close()
+    del pages
+    torch.cuda.empty_cache()
     for direction, mode, per_sm, frac in variants:
         if per_sm:
             _lib.configure(sm_ctas_dev=per_sm * sms)
