@@ -17,6 +17,19 @@ def test_set_option_accepts_known_names_and_rejects_others():
     assert lib.kvx_set_option(b"ce_streams", 0) == _lib.KVX_ERR_INVALID_ARGUMENT
     assert lib.kvx_set_option(b"ce_streams", 9) == _lib.KVX_ERR_INVALID_ARGUMENT
     assert lib.kvx_set_option(b"ce_max_copy", -1) == _lib.KVX_ERR_INVALID_ARGUMENT
+    for name, good, bad in ((b"bulk_waves", (1, 16), (0, 65)),
+                            (b"bulk_ctas_per_sm", (1, 2), (0, 3)),
+                            (b"vec_bytes", (16, 32), (8, 64)),
+                            (b"staging_bulk", (0, 1), ()),
+                            (b"host_bulk", (1, 0), ())):
+        for v in good:
+            assert lib.kvx_set_option(name, v) == 0, (name, v)
+        for v in bad:
+            assert lib.kvx_set_option(name, v) == _lib.KVX_ERR_INVALID_ARGUMENT, (name, v)
+    # back to the defaults the other tests expect
+    for name, v in ((b"bulk_waves", 16), (b"bulk_ctas_per_sm", 2), (b"vec_bytes", 32),
+                    (b"staging_bulk", 1), (b"host_bulk", 0)):
+        assert lib.kvx_set_option(name, v) == 0
     assert lib.kvx_set_option(b"no_such_knob", 1) == _lib.KVX_ERR_INVALID_ARGUMENT
     assert b"no_such_knob" in lib.kvx_last_error()
     assert lib.kvx_set_option(None, 1) == _lib.KVX_ERR_INVALID_ARGUMENT
