@@ -880,13 +880,17 @@ int run_ce_grid(DeviceState* st, const GridPlan& p, cudaStream_t s, const Tunabl
 }
 
 // One copy-engine copy per coalesced extent (no staging, no kernel).
+// `merge` coalesces neighbours that are contiguous on both sides; callers
+// whose copies may span several tensors (segments) and are not merged per
+// segment already pass false, since one copy-engine copy must stay inside one
+// allocation.
 int run_ce_extent(const std::vector<Copy>& copies, const std::vector<size_t>& waves,
-                  cudaStream_t s) {
+                  cudaStream_t s, bool merge = true) {
   size_t begin = 0;
   for (size_t end : waves) {
     std::vector<Copy> w(copies.begin() + begin, copies.begin() + end);
     begin = end;
-    coalesce(&w);
+    if (merge) coalesce(&w);
     for (const Copy& c : w)
       KVX_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(c.dst),
                                reinterpret_cast<const void*>(c.src), c.len,
@@ -904,15 +908,38 @@ std::vector<Copy> grid_copies(GridPlan p) {
   return v;
 }
 
-// The same copies ordered by source address and coalesced, for one
-// copy-engine copy per extent.  A grid plan's copies never conflict (distinct
-// targets, no overlap between the sides), so their order is free; the
-// entry-major expansion puts different segments next to each other, which
-// never coalesce, while consecutive blocks of one segment do.
+// The same copies for one copy-engine copy per extent: segment by segment,
+// entries in source order, neighbours coalesced only inside a segment.  A
+// grid plan's copies never conflict (distinct targets, no overlap between the
+// sides), so their order is free, and consecutive blocks of one segment merge
+// into one copy.  Copies are never merged across segments: two segment
+// tensors may sit next to each other in the virtual address space while
+// belonging to different allocations (or, on a peer, to different IPC
+// mappings), and one copy-engine copy must stay inside one allocation.
 std::vector<Copy> grid_extents(const GridPlan& p) {
-  std::vector<Copy> v = grid_copies(p);
-  std::sort(v.begin(), v.end(), [](const Copy& a, const Copy& b) { return a.src < b.src; });
-  coalesce(&v);
+  std::vector<uint32_t> order(p.entries.size());
+  for (uint32_t i = 0; i < order.size(); ++i) order[i] = i;
+  std::sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) {
+    const GridEntry& x = p.entries[a];
+    const GridEntry& y = p.entries[b];
+    return x.src_id != y.src_id ? x.src_id < y.src_id : x.off < y.off;
+  });
+  std::vector<Copy> v;
+  v.reserve(p.entries.size() * p.segs.size());
+  for (const GridSeg& g : p.segs) {
+    const size_t first = v.size();
+    for (uint32_t i : order) {
+      const GridEntry& e = p.entries[i];
+      if (e.len == 0) continue;
+      const Copy c{g.src_base + uint64_t(e.src_id) * g.src_stride + e.off,
+                   g.dst_base + uint64_t(e.dst_id) * g.dst_stride + e.off, e.len};
+      if (v.size() > first && v.back().src + v.back().len == c.src &&
+          v.back().dst + v.back().len == c.dst)
+        v.back().len += c.len;
+      else
+        v.push_back(c);
+    }
+  }
   return v;
 }
 
@@ -1061,7 +1088,7 @@ int execute_grid_host(DeviceState* st, GridPlan* p, const HostInfo& hi,
   } else if (mode == KVX_MODE_CE_EXTENT) {
     // (already set, ordered and coalesced, when AUTO chose direct copies)
     if (expanded.empty()) expanded = grid_extents(*p);
-    rc = run_ce_extent(expanded, {expanded.size()}, s);
+    rc = run_ce_extent(expanded, {expanded.size()}, s, /*merge=*/false);
   } else {
     return set_error(KVX_ERR_INVALID_ARGUMENT, "unknown transfer mode " + std::to_string(mode));
   }
@@ -1638,7 +1665,8 @@ int kvx_migrate_blocks(kvx_layout* source, kvx_layout* target, int64_t num_entri
   const Path path = local ? Path::kDevice : Path::kPeer;
   if (mode == KVX_MODE_CE || mode == KVX_MODE_CE_EXTENT) {
     if (grid) copies = grid_extents(gp);
-    rc = run_ce_extent(copies, grid ? std::vector<size_t>{copies.size()} : split_waves(copies), s);
+    rc = run_ce_extent(copies, grid ? std::vector<size_t>{copies.size()} : split_waves(copies), s,
+                       /*merge=*/false);
     mode = KVX_MODE_CE_EXTENT;
   } else if (mode == KVX_MODE_SM || mode == KVX_MODE_SM_BULK) {
     // TMA bulk copies also cross NVLink: plain (non-multicast) bulk loads

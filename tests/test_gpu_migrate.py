@@ -81,14 +81,23 @@ def test_copy_blocks_local_overlapping_ids(cuda, mode):
     sw.close()
 
 
-def _peer_worker(rank, world, q_out, q_in, page, blocks, layers, direction):
+def plan_ids(blocks, whole):
+    """The migrated ids: every block of every segment in order (whole), or
+    200 random blocks to 200 random places."""
+    if whole:
+        return list(range(blocks)), list(range(blocks))
+    g = torch.Generator().manual_seed(5)
+    return (torch.randperm(blocks, generator=g)[:200].tolist(),
+            torch.randperm(blocks, generator=g)[:200].tolist())
+
+
+def _peer_worker(rank, world, q_out, q_in, page, blocks, layers, direction, mode="auto",
+                 whole=False):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     pages = cache_pages(dev, layers, blocks, page, 100 + rank)
     sw = make(rank, page, pages)
-    g = torch.Generator().manual_seed(5)
-    sid = torch.randperm(blocks, generator=g)[:200].tolist()
-    did = torch.randperm(blocks, generator=g)[:200].tolist()
+    sid, did = plan_ids(blocks, whole)
     q_out.put(("handles", rank, sw.export_kvcache_mem_handles()))
     _, peer, handles = q_in.get(timeout=120)
     torch.cuda.synchronize()
@@ -96,13 +105,14 @@ def _peer_worker(rank, world, q_out, q_in, page, blocks, layers, direction):
         sw.register_kvcache_mem_handles(0, None, handles)
         src_snapshot = None
         if direction == "pull":
-            ev = sw.migrate_blocks([1], 0, sid, did, [None], direction="pull")
+            ev = sw.migrate_blocks([1], 0, sid, did, [None], direction="pull", mode=mode)
             ev.synchronize()
         q_out.put(("done", rank, None))
     else:
         sw.register_kvcache_mem_handles(1, None, handles)
         if direction == "push":
-            sw.migrate_blocks([1], 1, sid, did, [None], direction="push").synchronize()
+            sw.migrate_blocks([1], 1, sid, did, [None], direction="push",
+                              mode=mode).synchronize()
         q_out.put(("done", rank, None))
     q_in.get(timeout=120)  # both finished
     out = [p.cpu().numpy().tobytes() for p in pages] if rank == 1 else None
@@ -112,17 +122,23 @@ def _peer_worker(rank, world, q_out, q_in, page, blocks, layers, direction):
 
 
 @pytest.mark.multigpu
-@pytest.mark.parametrize("direction", ["pull", "push"])
-def test_two_gpu_migration(cuda, direction):
+@pytest.mark.parametrize("direction,mode,whole,blocks", [
+    ("pull", "auto", False, 512), ("push", "auto", False, 512),
+    # every block of every segment: the copy-engine form must not merge copies
+    # across two segments' allocations, even where they sit next to each other
+    ("pull", "ce_extent", True, 4096), ("push", "ce_extent", True, 4096),
+    ("pull", "sm_bulk", True, 4096), ("push", "sm_bulk", False, 512)])
+def test_two_gpu_migration(cuda, direction, mode, whole, blocks):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
-    page, blocks, layers = 16384, 512, 4
+    page, layers = 16384, 4
     q0, q1, qa, qb = ctx.Queue(), ctx.Queue(), ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_peer_worker, args=(0, 2, q0, qa, page, blocks, layers, direction)),
-             ctx.Process(target=_peer_worker, args=(1, 2, q1, qb, page, blocks, layers, direction))]
+    args = (page, blocks, layers, direction, mode, whole)
+    procs = [ctx.Process(target=_peer_worker, args=(0, 2, q0, qa) + args),
+             ctx.Process(target=_peer_worker, args=(1, 2, q1, qb) + args)]
     for p in procs:
         p.start()
     try:
@@ -146,9 +162,7 @@ def test_two_gpu_migration(cuda, direction):
     # expected: rank 1's pages with rank 0's selected blocks copied in
     src = cache_pages(torch.device("cuda", 0), layers, blocks, page, 100)
     dst = cache_pages(torch.device("cuda", 1), layers, blocks, page, 101)
-    g = torch.Generator().manual_seed(5)
-    sid = torch.randperm(blocks, generator=g)[:200].tolist()
-    did = torch.randperm(blocks, generator=g)[:200].tolist()
+    sid, did = plan_ids(blocks, whole)
     exp = expected_after(src, dst, sid, did, page)
     for e, b in zip(exp, got):
         assert e.tobytes() == b
