@@ -695,8 +695,7 @@ def _peer_copy_peak(dist_, sw, partner: int, direction: str, active: bool, strea
     return {"per_pair_gbs": best, "bytes": nbytes,
             "how": f"copy engine: one cudaMemcpyAsync per segment ({segments} x "
                    f"{blocks * page} B) between the mapped caches, issued by the active rank "
-                   "on the migration stream, best of 5 windows (one stream drives one copy "
-                   "engine, well below the SM kernels)"}
+                   f"on {streams} stream(s), best of 5 windows"}
 
 
 def _ipc_event_ordering(dist_, dev, sw, pages, page: int, plan, is_src: bool, partner: int,
