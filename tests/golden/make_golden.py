@@ -13,6 +13,9 @@ Fixtures:
   block_tables.json  BlockTable.transfer_entries / moved_group_blocks /
                      swap_metadata and CacheGroupRuntimeConfig extents from
                      block_manager.py (``ray`` stubbed; it is not used there)
+  block_allocator.json  BlockManager's free-block allocator (GPU free lists,
+                     CPU slabs) through a scripted sequence of reservations,
+                     frees, move reclaims and slab reclaims
   move_requests.json BlockManager.move_requests (block_manager.py:1355-1525)
                      run on a stub manager: request lists, reservations,
                      swap_blocks arguments, tables and move events per move
@@ -418,6 +421,118 @@ def gen_move_requests(bm) -> dict:
     return {"group_specs": group_specs, "scenarios": scenarios}
 
 
+# The operation script of block_allocator.json: interpreted by gen_block_allocator
+# on the reference's BlockManager and by tests/test_golden_block_allocator.py on
+# the mirror.  "from"/"take" pick ids out of an earlier reservation's result.
+SHAPE_A = [2, 16, 8, 128]   # 65,536-byte blocks
+SHAPE_B = [2, 16, 4, 128]   # 32,768-byte blocks
+ALLOC_OPS = [
+    {"op": "register", "engine": 0, "num_max_blocks": 40, "shape": SHAPE_A,
+     "groups": [["attention", 16, 16, None]]},
+    {"op": "register", "engine": 1, "num_max_blocks": 1, "shape": SHAPE_A,
+     "groups": [["attention", 16, 16, None]]},
+    {"op": "register", "engine": 2, "num_max_blocks": 8, "shape": SHAPE_A, "groups": []},
+    {"op": "reserve", "n": 10, "location": 0, "shape": SHAPE_A},
+    {"op": "reserve", "n": 7, "location": -1, "shape": SHAPE_A},
+    {"op": "reserve", "n": 3, "location": -1, "shape": SHAPE_B},
+    {"op": "reserve", "n": 6, "location": -1, "shape": SHAPE_A},
+    {"op": "free", "location": -1, "shape": SHAPE_A, "from": 4, "take": [0, 2, 5]},
+    {"op": "free", "location": 0, "shape": SHAPE_A, "from": 3, "take": [9, 1, 4]},
+    {"op": "reserve", "n": 5, "location": -1, "shape": SHAPE_A},
+    {"op": "reserve", "n": 4, "location": 0, "shape": SHAPE_A},
+    {"op": "moved", "location": -1, "shape": SHAPE_A, "from": 6, "take": [0, 1, 2, 3, 4, 5]},
+    {"op": "moved", "location": 0, "shape": SHAPE_A, "from": 10, "take": [3, 0]},
+    {"op": "slabs"},
+    {"op": "free", "location": -1, "shape": SHAPE_B, "from": 5, "take": [0, 1, 2]},
+    {"op": "slabs"},
+    {"op": "reserve", "n": 30, "location": 0, "shape": SHAPE_A},
+    {"op": "reserve", "n": 80, "location": -1, "shape": SHAPE_A},
+    {"op": "reserve", "n": 12, "location": -1, "shape": SHAPE_B},
+    {"op": "hold", "rid": 50, "location": 0, "shape": SHAPE_A, "from": 3, "take": [0]},
+    {"op": "register", "engine": 0, "num_max_blocks": 40, "shape": SHAPE_A,
+     "groups": [["attention", 16, 16, None]]},
+    {"op": "release", "rid": 50},
+    {"op": "register", "engine": 0, "num_max_blocks": 24, "shape": SHAPE_A,
+     "groups": [["attention", 16, 16, None]]},
+    {"op": "reserve", "n": 23, "location": 0, "shape": SHAPE_A},
+    {"op": "reserve", "n": 1, "location": 0, "shape": SHAPE_A},
+]
+ALLOC_SLABS = 6
+ALLOC_SLAB_BYTES = 300_000  # not a multiple of either block size: partial blocks at slab edges
+
+
+def gen_block_allocator(bm) -> dict:
+    """BlockManager's allocator (block_manager.py:580-620, 653-689, 718-792,
+    918-1031, 1264-1277) run through ALLOC_OPS: each step's result (ids, or
+    exception type and message) and the allocator state after it."""
+    import asyncio
+    from collections import deque
+
+    bm.CudaRTLibrary = lambda: None  # the allocator never touches the CUDA runtime
+    mgr = bm.BlockManager(ALLOC_SLABS, ALLOC_SLAB_BYTES)
+    results = []
+
+    def state():
+        return {
+            "gpu_free_blocks": {str(k): list(v) for k, v in sorted(mgr.gpu_free_blocks.items())},
+            "cpu_free_blocks": {str(list(k)): list(v)
+                                for k, v in sorted(mgr.cpu_free_blocks.items()) if v},
+            "cpu_free_slabs": list(mgr.cpu_free_slabs),
+            "cpu_slab_usage": list(mgr.cpu_slab_usage),
+            "cpu_block_shape": [None if x is None else list(x) for x in mgr.cpu_block_shape],
+            "gpu_num_max_blocks": {str(k): v for k, v in sorted(mgr.gpu_num_max_blocks.items())},
+        }
+
+    def table(loc, shape, blocks):
+        return bm.BlockTable(loc, tuple(shape), (bm.CacheGroupConfig("attention", 16, 16),),
+                             [list(blocks)])
+
+    next_rid = [1000]
+    steps = []
+    for op in ALLOC_OPS:
+        picked = None
+        if "from" in op:
+            src = results[op["from"]]
+            picked = [src[i] for i in op["take"]]
+        try:
+            kind = op["op"]
+            if kind == "register":
+                mgr.register_gpu_space(op["engine"], op["num_max_blocks"], tuple(op["shape"]),
+                                       [tuple(g) for g in op["groups"]], None)
+                out = None
+            elif kind == "reserve":
+                out = asyncio.run(mgr._get_free_blocks(op["n"], op["location"],
+                                                        tuple(op["shape"])))
+            elif kind == "free":
+                rid = next_rid[0]
+                next_rid[0] += 1
+                mgr.block_tables[rid] = table(op["location"], op["shape"], picked)
+                mgr.free_blocks(rid)
+                out = None
+            elif kind == "moved":
+                ev = bm.MoveEvent(0, [], tuple(op["shape"]), op["location"], 99, list(picked), [])
+                if op["location"] >= 0:
+                    out = mgr._reclaim_gpu_move_blocks_once(ev)
+                else:
+                    out = mgr._reclaim_cpu_move_blocks_once(ev)
+            elif kind == "slabs":
+                out = mgr._reclaim_cpu_slabs()
+            elif kind == "hold":
+                mgr.block_tables[op["rid"]] = table(op["location"], op["shape"], picked)
+                out = None
+            elif kind == "release":
+                mgr.free_blocks(op["rid"])
+                out = None
+            result = {"ok": out}
+        except Exception as e:  # noqa: BLE001 - the exception is the recorded result
+            out = None
+            result = {"error": type(e).__name__, "message": str(e)}
+        results.append(out)
+        steps.append({"op": op, "result": result, "state": state()})
+    assert isinstance(mgr.cpu_free_blocks[tuple(SHAPE_A)], deque)
+    return {"slabs": ALLOC_SLABS, "slab_bytes": ALLOC_SLAB_BYTES, "steps": steps}
+
+
 def main() -> None:
     if not os.path.isdir(os.path.join(REF, "aegaeon")):
         sys.exit(f"reference checkout not found at {REF}")
@@ -435,6 +550,7 @@ def main() -> None:
                 "block_tables.json": gen_block_tables(bm),
                 "swap_blocks.json": gen_swap_blocks(bm),
                 "move_requests.json": gen_move_requests(bm),
+                "block_allocator.json": gen_block_allocator(bm),
             }
         finally:
             os.chdir(cwd)
@@ -446,7 +562,10 @@ def main() -> None:
                            "block_tables.json": "aegaeon/block_manager.py",
                            "swap_blocks.json": "aegaeon/worker.py (Worker.swap_blocks)",
                            "move_requests.json": "aegaeon/block_manager.py "
-                                                 "(BlockManager.move_requests)"}[name],
+                                                 "(BlockManager.move_requests)",
+                           "block_allocator.json": "aegaeon/block_manager.py (BlockManager "
+                                                   "allocator: register_gpu_space, "
+                                                   "_get_free_blocks, free_blocks, reclaims)"}[name],
                        "data": data}, f, separators=(",", ":"))
         print(name, os.path.getsize(os.path.join(OUT, name)), "bytes")
 
