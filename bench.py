@@ -2262,7 +2262,7 @@ def run_config10(args):
     lists = [bench.step_lists(k) for k in range(args.warmup + args.steps)]
     hbm = measured_peaks().get("hbm_gbs", 6650.0)
 
-    def timed(tag, out):
+    def timed(tag, out, staging_bulk=True):
         for k in range(args.warmup):
             bench.issue(lists[k], args.mode)
         torch.cuda.synchronize()
@@ -2271,7 +2271,7 @@ def run_config10(args):
         t = bench.timed_device(args.steps, args.mode, lambda k: lists[args.warmup + k])
         _lib.kernel_timing(False)
         n_l, ms, busy, nbytes = _lib.kernel_timing_read()
-        iso = bench.kernel_roofline(mode_bulk=bool(_staging_bulk[0]))
+        iso = bench.kernel_roofline(mode_bulk=staging_bulk)
         out.setdefault(tag, []).append({
             "gbs": round(bench.bytes_per_step * args.steps / t / 1e9, 2),
             "kernel_frac": round(nbytes / (ms / 1e3) / 1e9 / hbm, 3) if ms else None,
@@ -2279,7 +2279,6 @@ def run_config10(args):
             "isolated_frac": round(iso["algorithmic_bytes"] / iso["seconds"] / 1e9 / hbm, 3),
             "launches": n_l})
 
-    _staging_bulk = [1]
 
     pieces = {}
     for piece_mib in (0, 256):
@@ -2299,8 +2298,7 @@ def run_config10(args):
                                               "bulk_waves": 16})):
         for k, v in opts.items():
             _lib.set_option(k, v)
-        _staging_bulk[0] = opts["staging_bulk"]
-        timed(tag, kernels)
+        timed(tag, kernels, staging_bulk=bool(opts["staging_bulk"]))
     _lib.set_option("staging_bulk", 1)
     _lib.set_option("bulk_ctas_per_sm", 2)
     _lib.set_option("bulk_waves", 16)
