@@ -111,3 +111,20 @@ def test_upload_weights_rejects_bad_arguments(cuda):
                                 one(ctypes.c_void_p, h.data_ptr()),
                                 one(ctypes.c_uint64, 4096), 1, 0, 1, None)
     assert rc == _lib.KVX_ERR_INVALID_ARGUMENT
+
+
+def test_upload_weights_mixed_sources_in_one_call(cuda):
+    """Page-locked and pageable storages (and an empty one) in one call: each
+    goes its own way (direct pieces or the bounce buffers), all bytes exact."""
+    torch.cuda.set_device(cuda)
+    rng = np.random.default_rng(51)
+    sizes = [(5 << 20) + 1, 0, (70 << 20) + 33, 4096, (3 << 20) + 7]
+    hosts = []
+    for k, n in enumerate(sizes):
+        t = torch.from_numpy(rng.integers(0, 256, n, dtype=np.uint8))
+        hosts.append(t.pin_memory() if k % 2 == 0 else t)
+    devs = [torch.zeros(n, dtype=torch.uint8, device=cuda) for n in sizes]
+    switch.upload_weights(list(zip(devs, hosts)), chunk_bytes=2 << 20, host_threads=3)
+    torch.cuda.synchronize()
+    for d, h in zip(devs, hosts):
+        assert torch.equal(d.cpu(), h)
