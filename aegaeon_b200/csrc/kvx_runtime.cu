@@ -77,7 +77,7 @@ constexpr int kMaxCeStreams = 8;
 
 struct Tunables {
   int64_t sm_ctas_host = 0;    // 0: number of SMs
-  int64_t sm_ctas_dev = 0;     // 0: 16 x number of SMs
+  int64_t sm_ctas_dev = 0;     // 0: by launch size, 4 to 16 x number of SMs
   // Mean coalesced host run from which AUTO stages through the copy engines.
   // Measured on B200 (896 KiB rows, scattered in groups): the copy engines
   // pay about 5 us per copy, so with ~1.2 MiB runs they reach 0.81 of the
@@ -94,11 +94,11 @@ struct Tunables {
   int64_t ce_pipeline = 0;  // double-buffered staging with a helper stream
   int64_t vec_bytes = 32;   // bytes per thread access of the vector kernel (16 or 32)
   int64_t bulk_ctas_per_sm = 2;  // CTAs per SM of the TMA kernel (1 or 2)
-  // TMA kernel grid = waves x resident CTAs.  Each CTA copies one contiguous
-  // span of the launch, so with a single wave the launch waits for the
-  // slowest of 296 spans; 16 waves of short spans balance themselves.
-  // Measured on B200 (1 GiB staging chunk): isolated 0.93 -> 1.00 of the
-  // copy peak, live beside the other direction's DMA 0.77 -> 0.85.
+  // Most waves of resident CTAs in a TMA kernel grid (bulk_grid).  Each CTA
+  // copies one contiguous span of the launch, so with a single wave the launch
+  // waits for the slowest of 296 spans; 16 waves of short spans balance
+  // themselves.  Measured on B200 (1 GiB staging chunk): isolated 0.93 ->
+  // 1.00 of the copy peak, live beside the other direction's DMA 0.77 -> 0.85.
   int64_t bulk_waves = 16;
   int64_t staging_bulk = 1;      // staging gather/scatter: 1 TMA kernel, 0 vector kernel
   int64_t inline_lists = 1;      // small grid plans passed in kernel parameters
@@ -362,10 +362,32 @@ enum class Path { kHostSrc, kHostDst, kDevice, kPeer };
 // (the TMA bulk kernel may serve these; host memory goes through the SMs).
 bool device_side(Path p) { return p == Path::kDevice || p == Path::kPeer; }
 
-int ctas_for(const DeviceState* st, Path p, const Tunables& tn) {
-  if (p == Path::kHostSrc || p == Path::kHostDst)
-    return int(tn.sm_ctas_host > 0 ? tn.sm_ctas_host : st->sms);
-  return int(tn.sm_ctas_dev > 0 ? tn.sm_ctas_dev : 16 * st->sms);
+// Grid of the vector kernel for a launch of n_tiles 32 KiB tiles.  Each CTA
+// copies one contiguous span of tiles.  With a host side: one CTA per SM (the
+// two directions' kernels must fit on the SMs together).  Device-only: about
+// 4 tiles per CTA, between 4 and 16 CTAs per SM (2 resident, so up to 8
+// waves): large launches get short spans that balance across the SMs, small
+// ones keep a few tiles per CTA.  An explicit setting overrides either.
+uint32_t vec_grid(const DeviceState* st, Path p, const Tunables& tn, uint32_t n_tiles) {
+  uint64_t ctas;
+  if (p == Path::kHostSrc || p == Path::kHostDst) {
+    ctas = tn.sm_ctas_host > 0 ? uint64_t(tn.sm_ctas_host) : uint64_t(st->sms);
+  } else if (tn.sm_ctas_dev > 0) {
+    ctas = uint64_t(tn.sm_ctas_dev);
+  } else {
+    ctas = std::min<uint64_t>(std::max<uint64_t>(n_tiles / 4, 4ull * st->sms), 16ull * st->sms);
+  }
+  return uint32_t(std::min<uint64_t>(n_tiles, ctas));
+}
+
+// Grid of the TMA bulk kernel for n_tiles 16 KiB chunks: about 8 chunks per
+// CTA (its 6-stage ring needs a few to pay for its set-up), at least one wave
+// of resident CTAs, at most bulk_waves waves.
+uint32_t bulk_grid(const DeviceState* st, const Tunables& tn, uint32_t n_tiles) {
+  const uint64_t resident = uint64_t(tn.bulk_ctas_per_sm) * uint64_t(st->sms);
+  const uint64_t cap = resident * uint64_t(std::max<int64_t>(tn.bulk_waves, 1));
+  const uint64_t ctas = std::min<uint64_t>(std::max<uint64_t>(n_tiles / 8, resident), cap);
+  return uint32_t(std::min<uint64_t>(n_tiles, ctas));
 }
 
 bool all_aligned16(const std::vector<Copy>& v) {
@@ -442,11 +464,10 @@ void launch_list(const List& list, const Launch& l, const DeviceState* st, cudaS
                  const Tunables& tn) {
   if (l.bulk) {
     // Up to two 96 KiB CTAs fit on an SM.
-    const uint32_t grid = std::min<uint32_t>(
-        l.n_tiles, uint32_t(tn.bulk_ctas_per_sm * st->sms * std::max<int64_t>(tn.bulk_waves, 1)));
+    const uint32_t grid = bulk_grid(st, tn, l.n_tiles);
     kvx_copy_bulk<List><<<grid, 32, kBulkSmem, s>>>(list, l.n_tiles);
   } else {
-    const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(ctas_for(st, l.path, tn)));
+    const uint32_t grid = vec_grid(st, l.path, tn, l.n_tiles);
     const bool host_src = l.path == Path::kHostSrc;
     if (tn.vec_bytes == 32) {
       if (host_src)
@@ -516,7 +537,7 @@ int launch_inline_as(const DeviceState* st, const GridPlan& p, const Launch& l, 
   list.n_segs = uint32_t(p.segs.size());
   std::memcpy(list.rec, p.entries.data(), p.entries.size() * sizeof(GridEntry));
   std::memcpy(list.rec + 2 * list.n, p.segs.data(), p.segs.size() * sizeof(GridSeg));
-  const uint32_t grid = std::min<uint32_t>(l.n_tiles, uint32_t(ctas_for(st, l.path, tn)));
+  const uint32_t grid = vec_grid(st, l.path, tn, l.n_tiles);
   const bool host_src = l.path == Path::kHostSrc;
   if (tn.vec_bytes == 32) {
     if (host_src)
