@@ -36,6 +36,18 @@ constexpr int kVecUnroll = 8;  // 256 threads x 8 x 16 B = 32 KiB per pass
 
 enum SrcKind : int { kSrcDevice = 0, kSrcHost = 1 };
 
+// CTAs of a vector-kernel launch with a host side.  Swap-out and swap-in
+// kernels run at the same time and must fit on the SMs together (two CTAs
+// per SM in all): 3/4 of the SM count for writes to host memory, 5/4 for
+// reads from it.  One direction alone moves the same bytes per second with
+// writes at 1/2 to 1 CTA per SM and reads at 3/4 to 3/2; with both
+// directions at once this split moves 0.80 of the bidirectional link where
+// one CTA per SM each way moves 0.70 (scattered 896 KiB host rows).
+inline uint32_t host_path_ctas(int sms, bool to_host) {
+  const int ctas = to_host ? sms * 3 / 4 : sms * 5 / 4;
+  return uint32_t(ctas > 0 ? ctas : 1);
+}
+
 __device__ __forceinline__ uint4 ld_dev16(const void* p) {
   uint4 r;
   asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"

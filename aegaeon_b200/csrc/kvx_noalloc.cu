@@ -183,7 +183,7 @@ int kvx_swap_noalloc(const int64_t* source_block_ids, const int64_t* target_bloc
   const uint64_t tiles = uint64_t(m) * tiles_per_block;
   int sms = 148;
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-  const uint32_t grid = uint32_t(std::min<uint64_t>(tiles, uint64_t(sms)));
+  const uint32_t grid = uint32_t(std::min<uint64_t>(tiles, host_path_ctas(sms, !is_swap_in)));
   const uint64_t cache = reinterpret_cast<uint64_t>(kv_cache);
   if (is_swap_in)
     kvx_copy_ids<kSrcHost><<<grid, kVecThreads, 0, s>>>(scratch, uint32_t(m), block_bytes,

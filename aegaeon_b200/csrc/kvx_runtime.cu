@@ -76,15 +76,16 @@ int from_plan(const Error& e) {
 constexpr int kMaxCeStreams = 8;
 
 struct Tunables {
-  int64_t sm_ctas_host = 0;    // 0: number of SMs
+  int64_t sm_ctas_host = 0;    // 0: by direction (3/4 of the SMs to host, 5/4 from host)
   int64_t sm_ctas_dev = 0;     // 0: by launch size, 4 to 16 x number of SMs
   // Mean coalesced host run from which AUTO stages through the copy engines.
   // Measured on B200 (896 KiB rows, scattered in groups): the copy engines
-  // pay about 5 us per copy, so with ~1.2 MiB runs they reach 0.81 of the
-  // link one way and 0.67 with both directions active, where the SM path
-  // holds 0.92 and 0.70; from ~2.3 MiB runs the copy engines win with both
-  // directions active (0.75 vs 0.71) and from ~4.7 MiB one way as well.
-  int64_t ce_min_run = 2ll << 20;
+  // pay about 5 us per copy, so with ~1.2 MiB runs they reach 0.82 of the
+  // link one way and 0.70 with both directions active, and 0.89 / 0.79 with
+  // ~2.3 MiB runs, where the SM path holds 0.92 and 0.85 at any run length;
+  // at ~4.7 MiB the two tie (0.93 / 0.85) and from ~9 MiB the copy engines
+  // win (0.95 / 0.89).
+  int64_t ce_min_run = 4ll << 20;
   // AUTO stages through the copy engines only from this payload up: below it
   // one zero-copy kernel beats gather + DMA (measured on B200: the SM path is
   // 3-17% faster from 0.5 to 8 MiB per call, the copy engines 3-6% faster at
@@ -363,15 +364,16 @@ enum class Path { kHostSrc, kHostDst, kDevice, kPeer };
 bool device_side(Path p) { return p == Path::kDevice || p == Path::kPeer; }
 
 // Grid of the vector kernel for a launch of n_tiles 32 KiB tiles.  Each CTA
-// copies one contiguous span of tiles.  With a host side: one CTA per SM (the
-// two directions' kernels must fit on the SMs together).  Device-only: about
-// 4 tiles per CTA, between 4 and 16 CTAs per SM (2 resident, so up to 8
-// waves): large launches get short spans that balance across the SMs, small
-// ones keep a few tiles per CTA.  An explicit setting overrides either.
+// copies one contiguous span of tiles.  With a host side: host_path_ctas (the
+// two directions' kernels share the SMs).  Device-only: about 4 tiles per
+// CTA, between 4 and 16 CTAs per SM (2 resident, so up to 8 waves): large
+// launches get short spans that balance across the SMs, small ones keep a
+// few tiles per CTA.  An explicit setting overrides either.
 uint32_t vec_grid(const DeviceState* st, Path p, const Tunables& tn, uint32_t n_tiles) {
   uint64_t ctas;
   if (p == Path::kHostSrc || p == Path::kHostDst) {
-    ctas = tn.sm_ctas_host > 0 ? uint64_t(tn.sm_ctas_host) : uint64_t(st->sms);
+    ctas = tn.sm_ctas_host > 0 ? uint64_t(tn.sm_ctas_host)
+                               : host_path_ctas(st->sms, p == Path::kHostDst);
   } else if (tn.sm_ctas_dev > 0) {
     ctas = uint64_t(tn.sm_ctas_dev);
   } else {

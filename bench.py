@@ -2208,7 +2208,7 @@ def run_config9(args):
     fs = FragSwap(dev, workloads.CFG3, 1024, 4096)
     peaks = host_link_peaks(dev)
     variants = [(True, 1, "auto", "auto", 0)]
-    for g in (1, 2, 8):
+    for g in (1, 2, 4, 8):
         for m in ("ce", "sm"):
             variants += [(True, g, m, m, 1), (True, g, m, None, 1), (True, g, None, m, 1)]
     variants += [(False, 1, "ce", "ce", 1), (False, 1, "sm", "sm", 1), (True, 1, "ce", "ce", 2)]

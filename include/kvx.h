@@ -57,7 +57,7 @@ extern "C" {
 #define KVX_MODE_AUTO 0     /* per-call choice by size and fragmentation:      */
                             /* at most 2 coalesced copies -> CE_EXTENT; host   */
                             /* memory not mapped -> CE; payload >= 16 MiB with */
-                            /* mean host run >= 2 MiB -> CE; otherwise SM       */
+                            /* mean host run >= 4 MiB -> CE; otherwise SM       */
 #define KVX_MODE_SM 1       /* SM kernel, 32-byte vector loads/stores; host    */
                             /* side through its device-mapped address          */
 #define KVX_MODE_CE 2       /* copy engines over coalesced runs; HBM side      */
@@ -287,7 +287,9 @@ int kvx_selftest_bounded_wait(uint64_t limit_ns, void* stream);
 
 /* Tuning knobs of KVX_MODE_AUTO and of the kernels; 0 keeps the current value
  * (ce_pipeline: -1 keeps it).
- *   sm_ctas_host : CTAs of an SM kernel that touches host memory
+ *   sm_ctas_host : CTAs of an SM kernel that touches host memory (default,
+ *                  and 0 through kvx_set_option: 3/4 of the SM count when it
+ *                  writes host memory, 5/4 when it reads it)
  *   sm_ctas_dev  : CTAs of an SM kernel that touches device memory only
  *   ce_min_run   : mean coalesced host-run bytes from which AUTO uses the CE
  *   staging_bytes: size of each staging area of the copy-engine mode
