@@ -1921,6 +1921,13 @@ def run_config6(args):
         cpu_pages = torch.empty((total, phys_bytes), dtype=torch.uint8).pin_memory()
         gpu = [torch.empty((total, seg_page), dtype=torch.uint8, device=dev)
                for _ in range(segments_n)]
+        # The first transfers over freshly page-locked memory run slower and
+        # this buffer is new for every length: one untimed round trip of the
+        # whole buffer first, the same for both arms.
+        scratch = cpu_pages.to(dev)
+        cpu_pages.copy_(scratch)
+        torch.cuda.synchronize()
+        del scratch
         segs = [swapper.CacheSegment(f"s{i}", (f"s{i}",), i * seg_page, seg_page)
                 for i in range(segments_n)]
         sw = None
