@@ -2118,10 +2118,13 @@ class FragSwap:
         return blocks[:n], rows[:n], rows[n:2 * n], blocks[n:2 * n]
 
     def run(self, steps: int, warmup: int, m_out, m_in, group: int = 1,
-            shuffled: bool = True, host_bulk=(False, False)) -> dict:
+            shuffled: bool = True, host_bulk=(False, False), ctas=None) -> dict:
         """Times `steps` steps (either direction may be None); returns GB/s
         of both directions together, the modes AUTO resolved to and whether
-        the last step's host rows and swapped-in blocks are exact."""
+        the last step's host rows and swapped-in blocks are exact.  `ctas`,
+        when given, sets `sm_ctas_host` for the swap-out and the swap-in
+        calls (and puts back the library's split by direction after each
+        step)."""
         import torch
 
         from aegaeon_b200 import _lib
@@ -2135,17 +2138,23 @@ class FragSwap:
             e_out = e_in = None
             if m_out:
                 _lib.set_option("host_bulk", int(host_bulk[0]))
+                if ctas:
+                    _lib.set_option("sm_ctas_host", ctas[0])
                 e_out = sw.swap_blocks([0], out_b, out_r, z, z, one, [None], False,
                                        mode="sm" if m_out == "smb" else m_out,
                                        stream=sw.swap_out_stream)
                 mo = _lib.last_mode_name() + ("+bulk" if host_bulk[0] else "")
             if m_in:
                 _lib.set_option("host_bulk", int(host_bulk[1]))
+                if ctas:
+                    _lib.set_option("sm_ctas_host", ctas[1])
                 e_in = sw.swap_blocks([1], in_r, in_b, z, z, one, [None], True,
                                       mode="sm" if m_in == "smb" else m_in,
                                       stream=sw.swap_in_stream)
                 mi = _lib.last_mode_name() + ("+bulk" if host_bulk[1] else "")
             _lib.set_option("host_bulk", 0)
+            if ctas:
+                _lib.set_option("sm_ctas_host", 0)
             if e_in is not None:
                 sw.swap_out_stream.wait_event(e_in)
             if e_out is not None:
@@ -2238,6 +2247,23 @@ def run_config9(args):
         out[key] = {"gbs": round(r["gbs"], 2), "frac": round(r["gbs"] / peak, 3),
                     "modes_used": r["modes_used"], "bit_exact": r["bit_exact"]}
     _lib.set_option("ce_streams", 1)
+    # both directions on the SMs, scattered rows: CTAs of the swap-out (host
+    # writes) and swap-in (host reads) kernels
+    for co, ci in ((148, 148), (74, 148), (96, 148), (111, 148), (96, 185), (111, 185),
+                   (80, 222), (48, 148), (74, 74)):
+        r = fs.run(args.steps, args.warmup, "sm", "sm", 1, True, ctas=(co, ci))
+        out[f"shuffled1:sm/sm:ctas{co}/{ci}"] = {
+            "gbs": round(r["gbs"], 2), "frac": round(r["gbs"] / peaks["bidir_gbs"], 3),
+            "modes_used": r["modes_used"], "bit_exact": r["bit_exact"]}
+    # the TMA bulk kernel both ways, sized so both directions stay resident
+    _lib.set_option("bulk_ctas_per_sm", 1)
+    _lib.set_option("bulk_waves", 1)
+    r = fs.run(args.steps, args.warmup, "smb", "smb", 1, True, host_bulk=(True, True))
+    _lib.set_option("bulk_ctas_per_sm", 2)
+    _lib.set_option("bulk_waves", 16)
+    out["shuffled1:smb/smb:1cta_per_sm_1wave"] = {
+        "gbs": round(r["gbs"], 2), "frac": round(r["gbs"] / peaks["bidir_gbs"], 3),
+        "modes_used": r["modes_used"], "bit_exact": r["bit_exact"]}
     fs.close()
     return {"impl": args.impl, "metric": METRIC, "value": out["shuffled1:auto/auto"]["gbs"],
             "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
