@@ -1388,11 +1388,17 @@ class Cfg1:
             else:
                 ops.swap(src, dst, is_in, cache, host, mode=mode)
 
-        def step(_k):
+        def step_out(_k):
             for c, h in zip(self.caches, self.hosts):
                 swap(self.out_ids, self.slots, False, c, h)
+
+        def step_in(_k):
             for c, h in zip(self.back, self.hosts):
                 swap(self.slots, self.in_ids, True, c, h)
+
+        def step(k):
+            step_out(k)
+            step_in(k)
 
         for k in range(warmup):
             step(k)
@@ -1400,13 +1406,21 @@ class Cfg1:
         t0 = time.perf_counter()
         t = _timed([], step, steps, self.dev)
         wall = time.perf_counter() - t0
+        # device time per call of each direction on its own (repeating a
+        # direction rewrites the same bytes, so the checks below still hold)
+        per_call = {}
+        if steps:
+            for name, fn in (("out", step_out), ("in", step_in)):
+                per_call[f"{name}_us_per_call"] = (_timed([], fn, steps, self.dev) * 1e6
+                                                   / steps / len(self.caches))
         oi = torch.tensor(self.out_ids, device=self.dev)
         ii = torch.tensor(self.in_ids, device=self.dev)
         exact = all(torch.equal(b[ii].view(torch.uint8), c[oi].view(torch.uint8)) and
                     torch.equal(h.to(self.dev).view(torch.uint8), c[oi].view(torch.uint8))
                     for b, c, h in zip(self.back, self.caches, self.hosts))
         return {"seconds": t, "wall": wall, "gbs": self.step_bytes * steps / t / 1e9,
-                "e2e_gbs": self.step_bytes * steps / wall / 1e9, "bit_exact": bool(exact)}
+                "e2e_gbs": self.step_bytes * steps / wall / 1e9, "bit_exact": bool(exact),
+                **per_call}
 
     def close(self):
         del self.caches, self.back, self.hosts
@@ -1746,7 +1760,8 @@ def run_config1(args):
               ref=_ref_module() if args.impl == "reference" else None)
     line = _line_for(args, r, "cfg1 Qwen3-4B round trip: 36 layers x separate K/V "
                      "[1024,16,8,128] bf16 N(0,1) seed 0; 256 blocks out to slots 0..255 then "
-                     "in to a fresh permutation, 72 swap calls per direction", args.impl)
+                     "in to a fresh permutation, 72 swap calls per direction", args.impl,
+                     {k: r[k] for k in ("out_us_per_call", "in_us_per_call") if k in r})
     line["e2e"].update({"h2d_bytes_per_step": c.step_bytes // 2,
                         "d2h_bytes_per_step": c.step_bytes // 2})
     return line
