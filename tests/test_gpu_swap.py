@@ -241,3 +241,40 @@ def test_staged_chunks_parity(cuda, oracle, pipeline):
 
 def test_device_status_clean(cuda):
     assert _lib.device_status(0) == 0
+
+
+@pytest.mark.parametrize("ctas", [0, 1, 3, 111, 185, 4096])
+@pytest.mark.parametrize("shape,dtype", [((64, 3, 5, 7), torch.bfloat16),
+                                         ((64, 16, 8, 128), torch.bfloat16),
+                                         ((32, 16, 32, 128), torch.float16)])
+def test_sm_host_path_any_grid_matches_oracle(cuda, oracle, ctas, shape, dtype):
+    """The SM zero-copy kernels split their tiles over however many CTAs the
+    host-path grid gives them (by default 3/4 of the SMs writing host memory
+    and 5/4 reading it; `sm_ctas_host` overrides both): one CTA, fewer CTAs
+    than tiles, more CTAs than tiles, and blocks of 210 bytes (byte path),
+    32 KiB (one tile) and 128 KiB (four tiles) all give the oracle's bytes."""
+    blocks = shape[0]
+    slots = blocks // 2 + 3
+    cache = rand_cache(shape, dtype, cuda, 21)
+    swap_buf = torch.empty((slots,) + shape[1:], dtype=dtype).pin_memory()
+    swap_buf.view(torch.uint8).fill_(0x3C)
+    bb = ops.reference_block_bytes(cache)
+    src, dst = perm(blocks, slots - 3, 22), perm(slots, slots - 3, 23)
+    back = perm(blocks, slots - 3, 24)
+    _lib.set_option("sm_ctas_host", ctas)
+    try:
+        exp_swap = host_bytes(swap_buf).copy()
+        oracle.swap(src, dst, False, host_bytes(cache.cpu()).copy(), exp_swap, bb)
+        ops.swap(src, dst, False, cache, swap_buf, mode="sm")
+        torch.cuda.synchronize()
+        assert _lib.last_mode_name() == "sm"
+        assert np.array_equal(host_bytes(swap_buf), exp_swap)
+        cache2 = torch.zeros_like(cache)
+        exp_cache = np.zeros(cache2.numel() * cache2.element_size(), np.uint8)
+        oracle.swap(dst, back, True, exp_cache, host_bytes(swap_buf).copy(), bb)
+        ops.swap(dst, back, True, cache2, swap_buf, mode="sm")
+        torch.cuda.synchronize()
+        assert np.array_equal(host_bytes(cache2.cpu()), exp_cache)
+    finally:
+        _lib.set_option("sm_ctas_host", 0)
+    assert _lib.device_status(cuda.index) == 0
