@@ -2281,6 +2281,8 @@ def run_config9(args):
         for m in ("ce", "sm"):
             variants += [(True, g, m, m, 1), (True, g, m, None, 1), (True, g, None, m, 1)]
     variants += [(False, 1, "ce", "ce", 1), (False, 1, "sm", "sm", 1), (True, 1, "ce", "ce", 2)]
+    # one mechanism per direction
+    variants += [(True, 1, "ce", "sm", 1), (True, 1, "sm", "ce", 1)]
     # SM mode through the TMA bulk kernel (16 KiB bulk copies to / from host rows)
     variants += [(True, 1, "smb", "smb", 1), (True, 1, "smb", None, 1), (True, 1, None, "smb", 1),
                  (True, 1, "smb", "sm", 1), (True, 1, "sm", "smb", 1),
