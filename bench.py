@@ -242,8 +242,10 @@ def host_link_peaks(dev, dist_=None) -> dict:
     pieces back to back (single multi-GiB copies run slower on this link),
     H2D alone, D2H alone, and both at once.  All ranks start each window after
     a barrier; a window's box figure is (bytes of all ranks) / (slowest
-    rank's device time).  Best of 5 windows after a warm-up; values returned
-    per GPU (box / N) plus the box figure of both directions."""
+    rank's device time).  Best of 10 windows after a warm-up (the host memory
+    is shared with other jobs, and a few short windows can all land in a busy
+    spell); values returned per GPU (box / N) plus the box figure of both
+    directions."""
     import torch
 
     world = dist_.world if dist_ is not None else 1
@@ -273,7 +275,7 @@ def host_link_peaks(dev, dist_=None) -> dict:
         fn()  # warm-up: first touch of the pages by the copy engines
         torch.cuda.synchronize()
         best = 0.0
-        for _ in range(5):
+        for _ in range(10):
             if dist_ is not None:
                 dist_.barrier()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -1117,7 +1119,8 @@ def run_kvx(args):
                 "frac": value / box_peak,
                 "peak_source": "measured live: every GPU of the run copies 2 GiB of "
                                "page-locked memory each way (256 MiB pieces) in the same "
-                               "barrier-started windows; box = all bytes / slowest rank; "
+                               "barrier-started windows, best of 10; box = all bytes / "
+                               "slowest rank; "
                                "per-GPU share shown (the step is bidirectional)",
                 "box_peak_gbs": box_peak,
                 "peak_h2d_gbs": peaks["h2d_gbs"],
