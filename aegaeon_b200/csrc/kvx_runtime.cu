@@ -77,6 +77,8 @@ constexpr int kMaxCeStreams = 8;
 
 struct Tunables {
   int64_t sm_ctas_host = 0;    // 0: by direction (3/4 of the SMs to host, 5/4 from host)
+  int64_t sm_ctas_host_out = 0;  // writes to host memory only; 0: sm_ctas_host's rule
+  int64_t sm_ctas_host_in = 0;   // reads from host memory only; 0: sm_ctas_host's rule
   int64_t sm_ctas_dev = 0;     // 0: by launch size, 4 to 16 x number of SMs
   // Mean coalesced host run from which AUTO stages through the copy engines.
   // Measured on B200 (896 KiB rows, scattered in groups): the copy engines
@@ -131,6 +133,8 @@ Tunables tunables() {
   std::call_once(once, [] {
     std::lock_guard<std::mutex> g(g_tun_mu);
     g_tun.sm_ctas_host = env_i64("KVX_SM_CTAS_HOST", g_tun.sm_ctas_host);
+    g_tun.sm_ctas_host_out = env_i64("KVX_SM_CTAS_HOST_OUT", g_tun.sm_ctas_host_out);
+    g_tun.sm_ctas_host_in = env_i64("KVX_SM_CTAS_HOST_IN", g_tun.sm_ctas_host_in);
     g_tun.sm_ctas_dev = env_i64("KVX_SM_CTAS_DEV", g_tun.sm_ctas_dev);
     g_tun.ce_min_run = env_i64("KVX_CE_MIN_RUN", g_tun.ce_min_run);
     g_tun.ce_min_bytes = env_i64("KVX_CE_MIN_BYTES", g_tun.ce_min_bytes);
@@ -368,12 +372,16 @@ bool device_side(Path p) { return p == Path::kDevice || p == Path::kPeer; }
 // two directions' kernels share the SMs).  Device-only: about 4 tiles per
 // CTA, between 4 and 16 CTAs per SM (2 resident, so up to 8 waves): large
 // launches get short spans that balance across the SMs, small ones keep a
-// few tiles per CTA.  An explicit setting overrides either.
+// few tiles per CTA.  An explicit setting overrides either (for a host side:
+// sm_ctas_host_out / sm_ctas_host_in before sm_ctas_host).
 uint32_t vec_grid(const DeviceState* st, Path p, const Tunables& tn, uint32_t n_tiles) {
   uint64_t ctas;
   if (p == Path::kHostSrc || p == Path::kHostDst) {
-    ctas = tn.sm_ctas_host > 0 ? uint64_t(tn.sm_ctas_host)
-                               : host_path_ctas(st->sms, p == Path::kHostDst);
+    const bool to_host = p == Path::kHostDst;
+    const int64_t one_way = to_host ? tn.sm_ctas_host_out : tn.sm_ctas_host_in;
+    ctas = one_way > 0              ? uint64_t(one_way)
+           : tn.sm_ctas_host > 0 ? uint64_t(tn.sm_ctas_host)
+                                 : host_path_ctas(st->sms, to_host);
   } else if (tn.sm_ctas_dev > 0) {
     ctas = uint64_t(tn.sm_ctas_dev);
   } else {
@@ -1424,6 +1432,10 @@ int kvx_set_option(const char* name, int64_t value) {
     g_tun.ce_min_bytes = value;
   } else if (n == "sm_ctas_host") {
     g_tun.sm_ctas_host = value;
+  } else if (n == "sm_ctas_host_out") {
+    g_tun.sm_ctas_host_out = value;
+  } else if (n == "sm_ctas_host_in") {
+    g_tun.sm_ctas_host_in = value;
   } else if (n == "sm_ctas_dev") {
     g_tun.sm_ctas_dev = value;
   } else if (n == "direct_max") {

@@ -317,7 +317,10 @@ int kvx_configure(int64_t sm_ctas_host, int64_t sm_ctas_dev,
  * mean host run is at most this many bytes; env KVX_CE_STREAMS_MAX_RUN),
  * "ce_max_copy" (largest single copy-engine copy of the staged mode; longer
  * host runs go as pieces of this size; 0 = no limit, env KVX_CE_MAX_COPY),
- * "ce_min_run", "ce_min_bytes", "sm_ctas_host", "sm_ctas_dev", "direct_max",
+ * "ce_min_run", "ce_min_bytes", "sm_ctas_host", "sm_ctas_host_out" and
+ * "sm_ctas_host_in" (CTAs of the SM kernel that writes host memory, or reads
+ * it; each overrides sm_ctas_host for its direction; 0: not set; env
+ * KVX_SM_CTAS_HOST_OUT / KVX_SM_CTAS_HOST_IN), "sm_ctas_dev", "direct_max",
  * "staging_bulk" (1: TMA bulk kernel for the staging gather/scatter, 0: the
  * vector kernel), "bulk_ctas_per_sm" (1 or 2), "bulk_waves" (1..64: the TMA
  * kernel's grid as this many waves of resident CTAs, 16 by default; env

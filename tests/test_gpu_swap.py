@@ -243,16 +243,17 @@ def test_device_status_clean(cuda):
     assert _lib.device_status(0) == 0
 
 
-@pytest.mark.parametrize("ctas", [0, 1, 3, 111, 185, 4096])
+@pytest.mark.parametrize("ctas", [0, 1, 3, 111, 185, 4096, (5, 300)])
 @pytest.mark.parametrize("shape,dtype", [((64, 3, 5, 7), torch.bfloat16),
                                          ((64, 16, 8, 128), torch.bfloat16),
                                          ((32, 16, 32, 128), torch.float16)])
 def test_sm_host_path_any_grid_matches_oracle(cuda, oracle, ctas, shape, dtype):
     """The SM zero-copy kernels split their tiles over however many CTAs the
     host-path grid gives them (by default 3/4 of the SMs writing host memory
-    and 5/4 reading it; `sm_ctas_host` overrides both): one CTA, fewer CTAs
-    than tiles, more CTAs than tiles, and blocks of 210 bytes (byte path),
-    32 KiB (one tile) and 128 KiB (four tiles) all give the oracle's bytes."""
+    and 5/4 reading it; `sm_ctas_host` overrides both, `sm_ctas_host_out` /
+    `sm_ctas_host_in` one direction each): one CTA, fewer CTAs than tiles,
+    more CTAs than tiles, and blocks of 210 bytes (byte path), 32 KiB (one
+    tile) and 128 KiB (four tiles) all give the oracle's bytes."""
     blocks = shape[0]
     slots = blocks // 2 + 3
     cache = rand_cache(shape, dtype, cuda, 21)
@@ -261,7 +262,11 @@ def test_sm_host_path_any_grid_matches_oracle(cuda, oracle, ctas, shape, dtype):
     bb = ops.reference_block_bytes(cache)
     src, dst = perm(blocks, slots - 3, 22), perm(slots, slots - 3, 23)
     back = perm(blocks, slots - 3, 24)
-    _lib.set_option("sm_ctas_host", ctas)
+    if isinstance(ctas, tuple):
+        _lib.set_option("sm_ctas_host_out", ctas[0])
+        _lib.set_option("sm_ctas_host_in", ctas[1])
+    else:
+        _lib.set_option("sm_ctas_host", ctas)
     try:
         exp_swap = host_bytes(swap_buf).copy()
         oracle.swap(src, dst, False, host_bytes(cache.cpu()).copy(), exp_swap, bb)
@@ -276,5 +281,6 @@ def test_sm_host_path_any_grid_matches_oracle(cuda, oracle, ctas, shape, dtype):
         torch.cuda.synchronize()
         assert np.array_equal(host_bytes(cache2.cpu()), exp_cache)
     finally:
-        _lib.set_option("sm_ctas_host", 0)
+        for name in ("sm_ctas_host", "sm_ctas_host_out", "sm_ctas_host_in"):
+            _lib.set_option(name, 0)
     assert _lib.device_status(cuda.index) == 0

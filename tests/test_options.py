@@ -13,7 +13,10 @@ def test_set_option_accepts_known_names_and_rejects_others():
     assert lib.kvx_set_option(b"ce_streams", 1) == 0
     assert lib.kvx_set_option(b"ce_max_copy", 256 << 20) == 0
     assert lib.kvx_set_option(b"ce_max_copy", 0) == 0
-    assert lib.kvx_set_option(b"ce_min_run", 2 << 20) == 0
+    assert lib.kvx_set_option(b"ce_min_run", 4 << 20) == 0
+    for name in (b"sm_ctas_host", b"sm_ctas_host_out", b"sm_ctas_host_in"):
+        assert lib.kvx_set_option(name, 96) == 0, name
+        assert lib.kvx_set_option(name, 0) == 0, name  # back to the split by direction
     assert lib.kvx_set_option(b"ce_streams", 0) == _lib.KVX_ERR_INVALID_ARGUMENT
     assert lib.kvx_set_option(b"ce_streams", 9) == _lib.KVX_ERR_INVALID_ARGUMENT
     assert lib.kvx_set_option(b"ce_max_copy", -1) == _lib.KVX_ERR_INVALID_ARGUMENT
